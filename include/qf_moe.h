@@ -1,0 +1,199 @@
+/*
+ * qf_moe.h -- C ABI of the B200 MoE-block library (libqf_moe.so).
+ *
+ * Drop-in boundary for the MoE step of QwenFieldfareCore.  In the reference
+ * (tanishqpatil/qwen-fieldfare, Swift + Metal) the "operator API" of this path
+ * is the Metal kernels' buffer-index ABI, encoded from Swift at
+ *   Sources/QwenFieldfareCore/Runtime/Generation/QwenQ4ActiveExpertStreamingRunner.swift:1169-1381
+ *   Sources/QwenFieldfareCore/Runtime/Generation/QwenQ4ChatRunner.swift:891-1000
+ * plus the Swift class Q4BoundedExpertCache
+ *   Sources/QwenFieldfareCore/Storage/Q4BoundedExpertCache.swift:14-419.
+ * Each entry point below names the reference kernel(s) or method it replaces.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, no CUDA or torch types.  Streams are passed
+ *     as `void*` (a cudaStream_t); NULL = the handle's stream.
+ *   - Device pointers are caller-owned (the reference caller owns every
+ *     MTLBuffer, kernels own nothing).  Calls are stream-ordered and
+ *     asynchronous; results are valid after the stream reaches them.
+ *   - Errors: every call returns qf_status; qf_last_error() returns the
+ *     message of the last failure on that handle.  No exceptions cross the
+ *     ABI.  A device-side status word (bounds/limit violations detected by
+ *     the kernels) is read by qf_moe_check().
+ *   - One handle per host thread (the reference runner is single-owner,
+ *     docs/AGENT_RUNTIME_PLAN.md:33).
+ *
+ * Weight layout (byte-exact with the reference):
+ *   expert record (1,769,472 B) = gate W | gate S | gate B | up W | up S | up B |
+ *                                 down W | down S | down B
+ *   at offsets 0, 524288, 557056, 589824, 1114112, 1146880, 1179648, 1703936,
+ *   1736704 (QwenQ4ExpertStoreBuilder.swift:47-56; deltanet.metal:2155-2211).
+ *   Q4 codes: element 2i is the low nibble of byte i; 64-column groups;
+ *   w = q*scale + bias with 16-bit scale/bias (fp16 or bf16).
+ *   Router: Q8 [256 x 2048] codes + [256 x 32] scales/biases; shared-expert
+ *   gate coefficient: Q8 [1 x 2048] (QwenQ4ActiveExpertStreamingRunner.swift:36-50).
+ */
+#ifndef QF_MOE_H
+#define QF_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QF_MOE_ABI_VERSION 1
+
+typedef enum qf_status {
+    QF_OK = 0,
+    QF_ERR_ARG = -1,         /* invalid argument / unsupported geometry */
+    QF_ERR_CUDA = -2,        /* CUDA runtime error */
+    QF_ERR_NCCL = -3,        /* collective error */
+    QF_ERR_OOM = -4,         /* allocation failed */
+    QF_ERR_IO = -5,          /* host tier / copy failure */
+    QF_ERR_TIMEOUT = -6,     /* a bounded device wait expired */
+    QF_ERR_DEVICE = -7,      /* device status word reported a violation */
+    QF_ERR_UNSUPPORTED = -8  /* feature not built for this configuration */
+} qf_status;
+
+typedef enum qf_scale_dtype { QF_SCALE_F16 = 0, QF_SCALE_BF16 = 1 } qf_scale_dtype;
+
+/* Geometry.  This build is specialised for the Qwen3.6-35B-A3B MoE block:
+ * hidden 2048, 256 experts, top-8, intermediate 512, group 64. */
+typedef struct qf_moe_dims {
+    int32_t hidden;
+    int32_t experts;
+    int32_t top_k;
+    int32_t intermediate;
+    int32_t group;
+    int32_t scale_dtype; /* qf_scale_dtype */
+} qf_moe_dims;
+
+/* One layer's MoE weights (device pointers).  Replaces the DenseLayerArena
+ * offsets routerW/S/B, shCoeffW/S/B, shGate..shDown
+ * (QwenQ4ActiveExpertStreamingRunner.swift:36-50) and the expert arena /
+ * cache buffer (Q4BoundedExpertCache.swift:23). */
+typedef struct qf_moe_layer {
+    const uint8_t *router_w;   /* [experts * hidden] Q8 codes */
+    const uint16_t *router_s;  /* [experts * hidden/64] */
+    const uint16_t *router_b;
+    const uint8_t *coef_w;     /* [hidden] Q8 codes of the shared-expert gate */
+    const uint16_t *coef_s;    /* [hidden/64] */
+    const uint16_t *coef_b;
+    const uint8_t *shared_record; /* one expert record: the shared expert */
+    const uint8_t *expert_bank;   /* record 0 of the routed bank / slot arena */
+    uint64_t record_stride;       /* bytes between records (>= 1,769,472, multiple of 16) */
+    uint32_t bank_records;        /* records in the bank (experts, or cache slots); a
+                                     routed record index >= this is a device error */
+    uint32_t reserved;            /* must be 0 */
+} qf_moe_layer;
+
+/* Routing controls.  All pointers are device pointers, may be NULL. */
+typedef struct qf_routing {
+    const float *logit_bias;       /* [experts] added to logits before top-k (harness) */
+    const int32_t *topk_idx;       /* [T * top_k] supplied expert ids (skip selection) */
+    const float *topk_w;           /* [T * top_k] supplied weights (with topk_idx) */
+    const int32_t *record_of_pos;  /* [T * top_k] bank record per routed position
+                                      (the cache's slot_indices); NULL: record = expert */
+} qf_routing;
+
+typedef struct qf_moe qf_moe;
+
+/* ---- handle ---------------------------------------------------------- */
+/* Replaces MetalContext (Infrastructure/Metal/MetalContext.swift:52-107). */
+qf_status qf_moe_create(const qf_moe_dims *dims, int device, qf_moe **out);
+void qf_moe_destroy(qf_moe *h);
+qf_status qf_moe_set_stream(qf_moe *h, void *stream);
+const char *qf_last_error(const qf_moe *h);
+/* Synchronises the handle's stream and returns the device status word
+ * (QF_OK, or QF_ERR_DEVICE/QF_ERR_TIMEOUT with the message set). */
+qf_status qf_moe_check(qf_moe *h);
+int qf_moe_abi_version(void);
+
+/* ---- kernels --------------------------------------------------------- */
+/* Router logits, Q8 affine.  Replaces qwen_router_q8_logits_simd_f32
+ * (deltanet.metal:2262-2281, dispatched at
+ * QwenQ4ActiveExpertStreamingRunner.swift:1178-1184).  Fixed reduction
+ * order: the reference's lane decomposition + xor-butterfly simd_sum, so the
+ * logits are bit-reproducible on the CPU.
+ *   x: fp16 [T * hidden]; logits: fp32 [T * experts]; coef (optional): fp32 [T]
+ *   (the shared-expert gate pre-activation, qwen_gemv_q8_affine rows=1,
+ *   deltanet.metal:863-902 / runner :1192-1200). */
+qf_status qf_router_logits_q8(qf_moe *h, const qf_moe_layer *layer, int32_t T,
+                              const uint16_t *x, float *logits, float *coef);
+
+/* Top-k by logit (ties to the lower expert index), softmax over all experts,
+ * renormalised over the top-k.  Replaces qwen_router_top8_logits_f32
+ * (deltanet.metal:2283-2329, dispatched at runner :1186-1190).
+ *   logits: fp32 [T * experts]; bias: fp32 [experts] or NULL;
+ *   idx: int32 [T * top_k]; w: fp32 [T * top_k]. */
+qf_status qf_router_topk(qf_moe *h, const float *logits, const float *bias, int32_t T,
+                         int32_t *idx, float *w);
+
+/* Stable dispatch plan (absent in the reference, which is decode-only):
+ * counts[experts], offsets[experts+1], perm[T*top_k] = position ids t*top_k+k
+ * sorted by (expert, t, k).  T <= 32768.  workspace: device scratch of at
+ * least qf_moe_dispatch_workspace_size bytes. */
+qf_status qf_moe_dispatch_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
+qf_status qf_moe_dispatch_plan(qf_moe *h, const int32_t *idx, int32_t T, int32_t *counts,
+                               int32_t *offsets, int32_t *perm, void *workspace,
+                               size_t workspace_bytes);
+
+/* Workspace bytes needed by qf_moe_block_forward / qf_moe_stack_forward at T tokens. */
+qf_status qf_moe_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
+
+/* One MoE block: out = residual + shared(x) + sum_k w_k * expert_k(x).
+ * Replaces the whole MoE step of forwardToken: router + top-8 + shared
+ * coefficient + shared gate/up/down + hit/miss subset gate/up/down + combine
+ * (deltanet.metal:2050-2227 as dispatched at
+ * QwenQ4ActiveExpertStreamingRunner.swift:1169-1381; resident variant
+ * deltanet.metal:1212-1411 at QwenQ4ChatRunner.swift:891-1000).
+ *   x: fp16 [T * hidden] post-norm hidden; residual: fp32 [T * hidden] or NULL;
+ *   out: fp32 [T * hidden]; idx_out/w_out: optional [T * top_k];
+ *   routing: optional; workspace: >= qf_moe_workspace_size bytes (256-B aligned).
+ * T in [1, 64] runs the decode kernels; larger T is rejected (QF_ERR_ARG)
+ * until the prefill path is built. */
+qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
+                               const uint16_t *x, const float *residual, float *out,
+                               const qf_routing *routing, int32_t *idx_out, float *w_out,
+                               void *workspace, size_t workspace_bytes);
+
+/* n_layers stacked blocks (the decode loop over 40 layers of forwardToken,
+ * runner :958).  Layer l reads x_l (fp16) and residual h_l; writes
+ * h_{l+1} = out_l; x_{l+1} = fp16(RMSNorm(out_l)) with unit weight and `eps`
+ * (qwen_rmsnorm_f32, deltanet.metal:18-53).  `layers` is a HOST array of
+ * n_layers descriptors.  idx_out/w_out (optional): [n_layers * T * top_k]. */
+qf_status qf_moe_stack_forward(qf_moe *h, const qf_moe_layer *layers, int32_t n_layers,
+                               int32_t T, const uint16_t *x, const float *residual, float *out,
+                               float eps, int32_t *idx_out, float *w_out, void *workspace,
+                               size_t workspace_bytes);
+
+/* ---- kernel timing (bench harness) ----------------------------------- */
+/* Records CUDA events around every launch of one kernel of the block
+ * (0 router, 1 top-k/grouping, 2 gate/up, 3 down, 4 combine) issued on this
+ * handle until qf_moe_profile_end, which synchronises and returns the summed
+ * duration of the first min(launches, max_launches) recorded launches.
+ * Launches captured into a CUDA graph report their most recent replay.
+ * (Counterpart of the reference's GPU profile, gpuStartTime/gpuEndTime,
+ * QwenQ4ActiveExpertStreamingRunner.swift:1486-1491.) */
+qf_status qf_moe_profile_begin(qf_moe *h, int32_t kernel_id, int32_t max_launches);
+qf_status qf_moe_profile_end(qf_moe *h, float *total_ms, int32_t *launches);
+
+/* ---- seeded synthetic data (bench/test harness) ---------------------- */
+/* Fills records for experts [expert0, expert0+count) of `layer` into
+ * bank + (expert - expert0) * stride (device memory).  expert id 256 is the
+ * shared expert.  Byte-identical to the CPU generator of the test oracle. */
+qf_status qf_synth_records(qf_moe *h, uint64_t seed, uint32_t layer, uint32_t expert0,
+                           uint32_t count, uint8_t *bank, uint64_t stride);
+qf_status qf_synth_router(qf_moe *h, uint64_t seed, uint32_t layer, uint8_t *w, uint16_t *s,
+                          uint16_t *b);
+qf_status qf_synth_coef(qf_moe *h, uint64_t seed, uint32_t layer, uint8_t *w, uint16_t *s,
+                        uint16_t *b);
+/* host memory: fp16 bits [T * 2048], N(0,1) then RMS-normalised */
+void qf_synth_hidden_host(uint64_t seed, uint64_t tok0, int32_t T, uint16_t *x);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QF_MOE_H */

@@ -1,0 +1,384 @@
+// qf_api.cu -- the C ABI declared in include/qf_moe.h: argument checks, device
+// selection, error text, and dispatch to the kernels.
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/qf_moe.h"
+#include "qf_internal.h"
+
+namespace qf {
+void prof_release(Prof* p);
+}
+using qf::prof_release;
+
+struct qf_moe {
+  int device;
+  qf_moe_dims dims;
+  cudaStream_t stream;
+  int* d_status;
+  std::string err;
+  qf::Prof prof;
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      ok = false;
+      return;
+    }
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+qf_status fail(qf_moe* h, qf_status s, const char* fmt, const char* a = "") {
+  if (h) {
+    char buf[512];
+    snprintf(buf, sizeof(buf), fmt, a);
+    h->err = buf;
+  }
+  return s;
+}
+
+qf_status cuda_fail(qf_moe* h, cudaError_t e, const char* where) {
+  if (h) h->err = std::string(where) + ": " + cudaGetErrorString(e);
+  return QF_ERR_CUDA;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+cudaStream_t stream_of(const qf_moe* h) { return h->stream; }
+
+qf_status layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
+  if (!l) return fail(h, QF_ERR_ARG, "layer descriptor is NULL");
+  if (!l->router_w || !l->router_s || !l->router_b || !l->coef_w || !l->coef_s || !l->coef_b ||
+      !l->shared_record || !l->expert_bank)
+    return fail(h, QF_ERR_ARG, "layer descriptor has a NULL weight pointer");
+  if (l->record_stride < qf::kRecordBytes || (l->record_stride % 16) != 0)
+    return fail(h, QF_ERR_ARG, "record_stride must be >= 1769472 and a multiple of 16");
+  if (!aligned(l->router_w, 16) || !aligned(l->coef_w, 16) || !aligned(l->shared_record, 16) ||
+      !aligned(l->expert_bank, 16) || !aligned(l->router_s, 2) || !aligned(l->router_b, 2) ||
+      !aligned(l->coef_s, 2) || !aligned(l->coef_b, 2))
+    return fail(h, QF_ERR_ARG, "weight pointers must be 16-byte aligned (codes, records)");
+  if (l->bank_records == 0 || l->bank_records >= (1u << 23))
+    return fail(h, QF_ERR_ARG, "bank_records must be in [1, 2^23)");
+  if (l->reserved != 0) return fail(h, QF_ERR_ARG, "reserved field must be 0");
+  w->rw = l->router_w;
+  w->rs = l->router_s;
+  w->rb = l->router_b;
+  w->cw = l->coef_w;
+  w->cs = l->coef_s;
+  w->cb = l->coef_b;
+  w->shared = l->shared_record;
+  w->bank = l->expert_bank;
+  w->stride = l->record_stride;
+  w->bank_records = l->bank_records;
+  return QF_OK;
+}
+
+qf_status routing_args(qf_moe* h, const qf_routing* r, qf::RoutingArgs* a) {
+  a->bias = nullptr;
+  a->idx_in = nullptr;
+  a->w_in = nullptr;
+  a->rec_of_pos = nullptr;
+  if (!r) return QF_OK;
+  if ((r->topk_idx == nullptr) != (r->topk_w == nullptr))
+    return fail(h, QF_ERR_ARG, "routing: topk_idx and topk_w must be given together");
+  a->bias = r->logit_bias;
+  a->idx_in = r->topk_idx;
+  a->w_in = r->topk_w;
+  a->rec_of_pos = r->record_of_pos;
+  return QF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qf_moe_abi_version(void) { return QF_MOE_ABI_VERSION; }
+
+qf_status qf_moe_create(const qf_moe_dims* dims, int device, qf_moe** out) {
+  if (!out) return QF_ERR_ARG;
+  *out = nullptr;
+  if (!dims) return QF_ERR_ARG;
+  if (dims->hidden != qf::kHidden || dims->experts != qf::kExperts || dims->top_k != qf::kTopK ||
+      dims->intermediate != qf::kInter || dims->group != qf::kGroup ||
+      (dims->scale_dtype != QF_SCALE_F16 && dims->scale_dtype != QF_SCALE_BF16))
+    return QF_ERR_ARG;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return QF_ERR_CUDA;
+  DeviceGuard g(device);
+  if (!g.ok) return QF_ERR_CUDA;
+  qf_moe* h = new qf_moe();
+  h->device = device;
+  h->dims = *dims;
+  h->stream = nullptr;
+  if (cudaMalloc(&h->d_status, 256) != cudaSuccess) {
+    delete h;
+    return QF_ERR_OOM;
+  }
+  if (cudaMemset(h->d_status, 0, 256) != cudaSuccess || qf::decode_init_attributes() != cudaSuccess) {
+    cudaFree(h->d_status);
+    delete h;
+    return QF_ERR_CUDA;
+  }
+  *out = h;
+  return QF_OK;
+}
+
+void qf_moe_destroy(qf_moe* h) {
+  if (!h) return;
+  DeviceGuard g(h->device);
+  prof_release(&h->prof);
+  cudaFree(h->d_status);
+  delete h;
+}
+
+qf_status qf_moe_set_stream(qf_moe* h, void* stream) {
+  if (!h) return QF_ERR_ARG;
+  h->stream = static_cast<cudaStream_t>(stream);
+  return QF_OK;
+}
+
+const char* qf_last_error(const qf_moe* h) {
+  if (!h) return "null handle";
+  return h->err.c_str();
+}
+
+qf_status qf_moe_check(qf_moe* h) {
+  if (!h) return QF_ERR_ARG;
+  DeviceGuard g(h->device);
+  cudaError_t e = cudaStreamSynchronize(stream_of(h));
+  if (e != cudaSuccess) return cuda_fail(h, e, "qf_moe_check: stream");
+  int st = 0;
+  e = cudaMemcpy(&st, h->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(h, e, "qf_moe_check: status");
+  if (st != 0) {
+    cudaMemset(h->d_status, 0, sizeof(int));
+    if (st == QF_ERR_TIMEOUT) return fail(h, QF_ERR_TIMEOUT, "a bounded device wait expired");
+    return fail(h, QF_ERR_DEVICE,
+                "device status: an index or record id was out of range (the access was skipped)");
+  }
+  return QF_OK;
+}
+
+qf_status qf_router_logits_q8(qf_moe* h, const qf_moe_layer* layer, int32_t T, const uint16_t* x,
+                              float* logits, float* coef) {
+  if (!h) return QF_ERR_ARG;
+  qf::LayerW w;
+  qf_status s = layer_to_w(h, layer, &w);
+  if (s != QF_OK) return s;
+  if (T < 1 || T > 65536) return fail(h, QF_ERR_ARG, "T must be in [1, 65536]");
+  if (!x || !logits || !aligned(x, 16)) return fail(h, QF_ERR_ARG, "x (16-B aligned) and logits are required");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::router_logits(stream_of(h), w, h->dims.scale_dtype == QF_SCALE_BF16, T, x,
+                                    logits, coef, h->d_status);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_router_logits_q8");
+}
+
+qf_status qf_router_topk(qf_moe* h, const float* logits, const float* bias, int32_t T, int32_t* idx,
+                         float* w) {
+  if (!h) return QF_ERR_ARG;
+  if (T < 1 || T > 65536) return fail(h, QF_ERR_ARG, "T must be in [1, 65536]");
+  if (!logits || !idx || !w) return fail(h, QF_ERR_ARG, "logits, idx and w are required");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::router_topk(stream_of(h), T, logits, bias, idx, w, h->d_status);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_router_topk");
+}
+
+qf_status qf_moe_dispatch_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
+  if (!h || !bytes) return QF_ERR_ARG;
+  if (T < 1 || T > 32768) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
+  *bytes = qf::dispatch_workspace_bytes(T);
+  return QF_OK;
+}
+
+qf_status qf_moe_dispatch_plan(qf_moe* h, const int32_t* idx, int32_t T, int32_t* counts,
+                               int32_t* offsets, int32_t* perm, void* workspace,
+                               size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  if (T < 1 || T > 32768) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
+  if (!idx || !counts || !offsets || !perm) return fail(h, QF_ERR_ARG, "idx/counts/offsets/perm required");
+  if (!workspace || workspace_bytes < qf::dispatch_workspace_bytes(T) || !aligned(workspace, 16))
+    return fail(h, QF_ERR_ARG, "workspace too small or misaligned");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::dispatch_plan_ws(stream_of(h), idx, T, counts, offsets, perm,
+                                       static_cast<int*>(workspace), h->d_status);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_dispatch_plan");
+}
+
+qf_status qf_moe_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
+  if (!h || !bytes) return QF_ERR_ARG;
+  if (T < 1 || T > qf::kDecodeMaxTokens)
+    return fail(h, QF_ERR_ARG, "T must be in [1, 64] for the decode path");
+  *bytes = qf::decode_workspace_bytes(T);
+  return QF_OK;
+}
+
+qf_status qf_moe_block_forward(qf_moe* h, const qf_moe_layer* layer, int32_t T, const uint16_t* x,
+                               const float* residual, float* out, const qf_routing* routing,
+                               int32_t* idx_out, float* w_out, void* workspace,
+                               size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  qf::LayerW w;
+  qf_status s = layer_to_w(h, layer, &w);
+  if (s != QF_OK) return s;
+  if (T < 1 || T > qf::kDecodeMaxTokens)
+    return fail(h, QF_ERR_ARG, "T must be in [1, 64] (decode path)");
+  if (!x || !out || !aligned(x, 16)) return fail(h, QF_ERR_ARG, "x (16-B aligned) and out are required");
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::decode_workspace_bytes(T))
+    return fail(h, QF_ERR_ARG, "workspace too small or not 256-byte aligned");
+  qf::RoutingArgs r;
+  s = routing_args(h, routing, &r);
+  if (s != QF_OK) return s;
+  qf::DecodeWs ws;
+  qf::decode_carve(workspace, T, &ws);
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::decode_block(stream_of(h), w, h->dims.scale_dtype == QF_SCALE_BF16, T, x,
+                                   residual, out, r, idx_out, w_out, ws, nullptr, 0.f, h->d_status,
+                                   &h->prof);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_block_forward");
+}
+
+qf_status qf_moe_stack_forward(qf_moe* h, const qf_moe_layer* layers, int32_t n_layers, int32_t T,
+                               const uint16_t* x, const float* residual, float* out, float eps,
+                               int32_t* idx_out, float* w_out, void* workspace,
+                               size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  if (!layers || n_layers < 1) return fail(h, QF_ERR_ARG, "layers array and n_layers >= 1 required");
+  if (T < 1 || T > qf::kDecodeMaxTokens)
+    return fail(h, QF_ERR_ARG, "T must be in [1, 64] (decode path)");
+  if (!x || !out || !aligned(x, 16)) return fail(h, QF_ERR_ARG, "x (16-B aligned) and out are required");
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::decode_workspace_bytes(T))
+    return fail(h, QF_ERR_ARG, "workspace too small or not 256-byte aligned");
+  if (!(eps > 0.f)) return fail(h, QF_ERR_ARG, "eps must be > 0");
+  qf::DecodeWs ws;
+  qf::decode_carve(workspace, T, &ws);
+  qf::RoutingArgs r = {nullptr, nullptr, nullptr, nullptr};
+  DeviceGuard g(h->device);
+  const bool bf16 = h->dims.scale_dtype == QF_SCALE_BF16;
+  const size_t PT = static_cast<size_t>(T) * qf::kTopK;
+  for (int l = 0; l < n_layers; l++) {
+    qf::LayerW w;
+    qf_status s = layer_to_w(h, &layers[l], &w);
+    if (s != QF_OK) return s;
+    const int cur = l & 1;
+    const uint16_t* xin = (l == 0) ? x : ws.x16[cur];
+    const float* res = (l == 0) ? residual : ws.h[cur];
+    float* o = (l == n_layers - 1) ? out : ws.h[cur ^ 1];
+    uint16_t* xn = (l == n_layers - 1) ? nullptr : ws.x16[cur ^ 1];
+    cudaError_t e = qf::decode_block(stream_of(h), w, bf16, T, xin, res, o, r,
+                                     idx_out ? idx_out + l * PT : nullptr,
+                                     w_out ? w_out + l * PT : nullptr, ws, xn, eps, h->d_status,
+                                     &h->prof);
+    if (e != cudaSuccess) return cuda_fail(h, e, "qf_moe_stack_forward");
+  }
+  return QF_OK;
+}
+
+qf_status qf_synth_records(qf_moe* h, uint64_t seed, uint32_t layer, uint32_t expert0,
+                           uint32_t count, uint8_t* bank, uint64_t stride) {
+  if (!h) return QF_ERR_ARG;
+  if (!bank || count == 0 || stride < qf::kRecordBytes || stride % 16 || !aligned(bank, 16) ||
+      expert0 + count > 257u)
+    return fail(h, QF_ERR_ARG, "bad synth_records arguments");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::synth_records(stream_of(h), seed, layer, expert0, count, bank, stride,
+                                    h->dims.scale_dtype == QF_SCALE_BF16);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_synth_records");
+}
+
+qf_status qf_synth_router(qf_moe* h, uint64_t seed, uint32_t layer, uint8_t* w, uint16_t* s,
+                          uint16_t* b) {
+  if (!h) return QF_ERR_ARG;
+  if (!w || !s || !b || !aligned(w, 8) || !aligned(s, 2) || !aligned(b, 2))
+    return fail(h, QF_ERR_ARG, "bad synth_router arguments");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::synth_q8(stream_of(h), seed, layer, true, w, s, b,
+                               h->dims.scale_dtype == QF_SCALE_BF16);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_synth_router");
+}
+
+qf_status qf_synth_coef(qf_moe* h, uint64_t seed, uint32_t layer, uint8_t* w, uint16_t* s,
+                        uint16_t* b) {
+  if (!h) return QF_ERR_ARG;
+  if (!w || !s || !b || !aligned(w, 8) || !aligned(s, 2) || !aligned(b, 2))
+    return fail(h, QF_ERR_ARG, "bad synth_coef arguments");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::synth_q8(stream_of(h), seed, layer, false, w, s, b,
+                               h->dims.scale_dtype == QF_SCALE_BF16);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_synth_coef");
+}
+
+}  // extern "C"
+
+void qf::prof_release(qf::Prof* p) {
+  for (int i = 0; i < p->cap; i++) {
+    cudaEventDestroy(p->ev0[i]);
+    cudaEventDestroy(p->ev1[i]);
+  }
+  delete[] p->ev0;
+  delete[] p->ev1;
+  *p = qf::Prof();
+}
+
+extern "C" {
+
+qf_status qf_moe_profile_begin(qf_moe* h, int32_t kernel_id, int32_t max_launches) {
+  if (!h) return QF_ERR_ARG;
+  if (kernel_id < 0 || kernel_id > 4 || max_launches < 1 || max_launches > 65536)
+    return fail(h, QF_ERR_ARG, "kernel_id in [0,4], max_launches in [1,65536]");
+  DeviceGuard g(h->device);
+  prof_release(&h->prof);
+  h->prof.ev0 = new cudaEvent_t[max_launches];
+  h->prof.ev1 = new cudaEvent_t[max_launches];
+  for (int i = 0; i < max_launches; i++) {
+    if (cudaEventCreate(&h->prof.ev0[i]) != cudaSuccess ||
+        cudaEventCreate(&h->prof.ev1[i]) != cudaSuccess) {
+      h->prof.cap = i;
+      prof_release(&h->prof);
+      return fail(h, QF_ERR_CUDA, "cudaEventCreate failed");
+    }
+  }
+  h->prof.cap = max_launches;
+  h->prof.n = 0;
+  h->prof.kernel = kernel_id;
+  return QF_OK;
+}
+
+qf_status qf_moe_profile_end(qf_moe* h, float* total_ms, int32_t* launches) {
+  if (!h || !total_ms || !launches) return QF_ERR_ARG;
+  DeviceGuard g(h->device);
+  float tot = 0.f;
+  const int n = h->prof.n;
+  for (int i = 0; i < n; i++) {
+    cudaError_t e = cudaEventSynchronize(h->prof.ev1[i]);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, h->prof.ev0[i], h->prof.ev1[i]);
+    if (e != cudaSuccess) {
+      prof_release(&h->prof);
+      return cuda_fail(h, e, "qf_moe_profile_end");
+    }
+    tot += ms;
+  }
+  prof_release(&h->prof);
+  *total_ms = tot;
+  *launches = n;
+  return QF_OK;
+}
+
+void qf_synth_hidden_host(uint64_t seed, uint64_t tok0, int32_t T, uint16_t* x) {
+  if (!x || T < 1) return;
+  qf::synth_hidden_host(seed, tok0, T, x);
+}
+
+}  // extern "C"

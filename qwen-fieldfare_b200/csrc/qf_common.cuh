@@ -1,0 +1,97 @@
+// qf_common.cuh -- geometry, record layout and small device helpers shared by
+// the MoE-block kernels.  Geometry is the Qwen3.6-35B-A3B MoE block used by
+// tanishqpatil/qwen-fieldfare (hidden 2048, 256 experts, top-8, intermediate
+// 512, Q4/Q8 MLX affine with 64-column groups).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qf {
+
+constexpr int kHidden = 2048;
+constexpr int kExperts = 256;
+constexpr int kTopK = 8;
+constexpr int kInter = 512;
+constexpr int kGroup = 64;
+constexpr int kSharedExpert = 256;  // expert id of the shared expert in generators
+constexpr uint64_t kRecordBytes = 1769472ull;
+
+// Byte offsets inside one expert record: the slot layout of the reference's
+// expert arena (QwenQ4ExpertStoreBuilder.swift:47-56, deltanet.metal:2155-2211).
+constexpr uint32_t kOffGateW = 0u;
+constexpr uint32_t kOffGateS = 524288u;
+constexpr uint32_t kOffGateB = 557056u;
+constexpr uint32_t kOffUpW = 589824u;
+constexpr uint32_t kOffUpS = 1114112u;
+constexpr uint32_t kOffUpB = 1146880u;
+constexpr uint32_t kOffDownW = 1179648u;
+constexpr uint32_t kOffDownS = 1703936u;
+constexpr uint32_t kOffDownB = 1736704u;
+
+// Decode path limits: T tokens, T*8 routed positions.
+constexpr int kDecodeMaxTokens = 64;
+constexpr int kMaxPositions = kDecodeMaxTokens * kTopK;  // 512
+
+// Device status word values (mirrors qf_status).
+constexpr int kStatusOk = 0;
+constexpr int kStatusDevice = -7;
+
+struct LayerW {
+  const uint8_t* rw;
+  const uint16_t* rs;
+  const uint16_t* rb;
+  const uint8_t* cw;
+  const uint16_t* cs;
+  const uint16_t* cb;
+  const uint8_t* shared;
+  const uint8_t* bank;
+  uint64_t stride;
+  uint32_t bank_records;
+};
+
+template <bool BF16>
+__device__ __forceinline__ float ld16(const uint16_t* p, int i) {
+  const uint16_t u = __ldg(p + i);
+  if constexpr (BF16) {
+    return __uint_as_float(static_cast<uint32_t>(u) << 16);
+  } else {
+    return __half2float(__ushort_as_half(u));
+  }
+}
+
+// xor-butterfly simd_sum (16, 8, 4, 2, 1): every lane ends with the same value,
+// and the order is the one the CPU oracle reproduces.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+
+// q (0..15) of nibble k of a packed word, as an exact float.
+__device__ __forceinline__ float nib(uint32_t w, int k) {
+  return __uint_as_float(0x4B000000u | ((w >> (4 * k)) & 0xFu)) - 8388608.0f;
+}
+// byte k of a packed word, as an exact float.
+__device__ __forceinline__ float byte_f(uint32_t w, int k) {
+  return __uint_as_float(0x4B000000u | ((w >> (8 * k)) & 0xFFu)) - 8388608.0f;
+}
+
+// word d (compile-time after unrolling) of a 16-byte vector, without taking
+// the vector's address (which would force it into local memory).
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int d) {
+  return d == 0 ? v.x : (d == 1 ? v.y : (d == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ void set_status(int* status, int code) {
+  if (status) atomicCAS(status, kStatusOk, code);
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  // SiLU(g) * u as in deltanet.metal:4-6 (x / (1 + e^-x)); expf is CUDA's.
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+}  // namespace qf

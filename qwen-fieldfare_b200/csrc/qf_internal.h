@@ -1,0 +1,76 @@
+// qf_internal.h -- host-side declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "qf_common.cuh"
+
+namespace qf {
+
+// ---- synthetic data (qf_synth.cu)
+cudaError_t synth_records(cudaStream_t st, uint64_t seed, uint32_t layer, uint32_t expert0,
+                          uint32_t count, uint8_t* bank, uint64_t stride, bool bf16);
+cudaError_t synth_q8(cudaStream_t st, uint64_t seed, uint32_t layer, bool router, uint8_t* w,
+                     uint16_t* s, uint16_t* b, bool bf16);
+void synth_hidden_host(uint64_t seed, uint64_t tok0, int T, uint16_t* x);
+
+// ---- decode path (qf_decode.cu)
+struct DecodeWs {
+  float* logits;      // [T, 256]
+  float* coef;        // [T]
+  int* idx;           // [T, 8]
+  float* w;           // [T, 8]
+  int* meta;          // [0] = n_groups
+  int* group_rec;     // [512]
+  int* group_start;   // [512]
+  int* group_cnt;     // [512]
+  int* sorted_pos;    // [512]
+  float* act;         // [T*8, 512]
+  float* act_sh;      // [T, 512]
+  float* y_part;      // [T*8, 2048]
+  float* y_sh;        // [T, 2048]
+  float* h[2];        // stack residual ping-pong [T, 2048]
+  uint16_t* x16[2];   // stack input ping-pong [T, 2048]
+};
+
+size_t decode_workspace_bytes(int T);
+void decode_carve(void* base, int T, DecodeWs* ws);
+cudaError_t decode_init_attributes();
+
+// Event pairs recorded around launches of one kernel (bench timing).
+struct Prof {
+  int kernel = -1;  // -1: off
+  int cap = 0;
+  int n = 0;
+  cudaEvent_t* ev0 = nullptr;
+  cudaEvent_t* ev1 = nullptr;
+};
+enum KernelId { kKRouter = 0, kKTopk = 1, kKGateUp = 2, kKDown = 3, kKCombine = 4 };
+
+struct RoutingArgs {
+  const float* bias;
+  const int* idx_in;
+  const float* w_in;
+  const int* rec_of_pos;
+};
+
+// One block: launches router, top-k/grouping, gate/up, down, combine.
+// x16_next (optional): fp16 RMSNorm of the output for a following block.
+cudaError_t decode_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                         const float* residual, float* out, const RoutingArgs& r, int* idx_out,
+                         float* w_out, const DecodeWs& ws, uint16_t* x16_next, float eps,
+                         int* status, Prof* prof);
+
+cudaError_t router_logits(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                          float* logits, float* coef, int* status);
+cudaError_t router_topk(cudaStream_t st, int T, const float* logits, const float* bias,
+                        int* idx, float* w, int* status);
+
+// ---- dispatch plan (qf_route.cu)
+size_t dispatch_workspace_bytes(int T);
+cudaError_t dispatch_plan_ws(cudaStream_t st, const int* idx, int T, int* counts, int* offsets,
+                             int* perm, int* scratch, int* status);
+
+}  // namespace qf

@@ -1,0 +1,98 @@
+"""Loads libqf_moe.so (built in-tree by the package Makefile) and declares the
+C ABI of include/qf_moe.h for ctypes.
+
+There is no fallback: if the library is missing or fails to load, every entry
+point raises.  The MoE block only runs through the sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libqf_moe.so")
+
+QF_OK = 0
+STATUS_NAMES = {
+    0: "QF_OK", -1: "QF_ERR_ARG", -2: "QF_ERR_CUDA", -3: "QF_ERR_NCCL", -4: "QF_ERR_OOM",
+    -5: "QF_ERR_IO", -6: "QF_ERR_TIMEOUT", -7: "QF_ERR_DEVICE", -8: "QF_ERR_UNSUPPORTED",
+}
+
+
+class QfError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+class MoEDims(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("experts", C.c_int32), ("top_k", C.c_int32),
+                ("intermediate", C.c_int32), ("group", C.c_int32), ("scale_dtype", C.c_int32)]
+
+
+class MoELayerDesc(C.Structure):
+    _fields_ = [("router_w", C.c_void_p), ("router_s", C.c_void_p), ("router_b", C.c_void_p),
+                ("coef_w", C.c_void_p), ("coef_s", C.c_void_p), ("coef_b", C.c_void_p),
+                ("shared_record", C.c_void_p), ("expert_bank", C.c_void_p),
+                ("record_stride", C.c_uint64), ("bank_records", C.c_uint32),
+                ("reserved", C.c_uint32)]
+
+
+class RoutingDesc(C.Structure):
+    _fields_ = [("logit_bias", C.c_void_p), ("topk_idx", C.c_void_p), ("topk_w", C.c_void_p),
+                ("record_of_pos", C.c_void_p)]
+
+
+# (name, restype, argtypes) for every symbol include/qf_moe.h declares.
+_P = C.c_void_p
+_I = C.c_int32
+_S = C.c_int  # qf_status
+SIGNATURES = {
+    "qf_moe_abi_version": (C.c_int, []),
+    "qf_moe_create": (_S, [C.POINTER(MoEDims), C.c_int, C.POINTER(_P)]),
+    "qf_moe_destroy": (None, [_P]),
+    "qf_moe_set_stream": (_S, [_P, _P]),
+    "qf_last_error": (C.c_char_p, [_P]),
+    "qf_moe_check": (_S, [_P]),
+    "qf_router_logits_q8": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P]),
+    "qf_router_topk": (_S, [_P, _P, _P, _I, _P, _P]),
+    "qf_moe_dispatch_workspace_size": (_S, [_P, _I, C.POINTER(C.c_size_t)]),
+    "qf_moe_dispatch_plan": (_S, [_P, _P, _I, _P, _P, _P, _P, C.c_size_t]),
+    "qf_moe_workspace_size": (_S, [_P, _I, C.POINTER(C.c_size_t)]),
+    "qf_moe_block_forward": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
+                                  C.POINTER(RoutingDesc), _P, _P, _P, C.c_size_t]),
+    "qf_moe_stack_forward": (_S, [_P, C.POINTER(MoELayerDesc), _I, _I, _P, _P, _P, C.c_float,
+                                  _P, _P, _P, C.c_size_t]),
+    "qf_moe_profile_begin": (_S, [_P, _I, _I]),
+    "qf_moe_profile_end": (_S, [_P, C.POINTER(C.c_float), C.POINTER(_I)]),
+    "qf_synth_records": (_S, [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _P,
+                              C.c_uint64]),
+    "qf_synth_router": (_S, [_P, C.c_uint64, C.c_uint32, _P, _P, _P]),
+    "qf_synth_coef": (_S, [_P, C.c_uint64, C.c_uint32, _P, _P, _P]),
+    "qf_synth_hidden_host": (None, [C.c_uint64, C.c_uint64, _I, _P]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded library; raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `make -C qwen-fieldfare_b200` "
+                "(or __graft_entry__.build()); the MoE path has no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, handle=None) -> None:
+    if status != QF_OK:
+        msg = lib().qf_last_error(handle).decode() if handle else ""
+        raise QfError(status, msg)

@@ -169,6 +169,25 @@ qf_status qf_moe_stack_forward(qf_moe *h, const qf_moe_layer *layers, int32_t n_
                                float eps, int32_t *idx_out, float *w_out, void *workspace,
                                size_t workspace_bytes);
 
+/* Allocation-free variant of qf_moe_block_forward (no counterpart in the
+ * reference, whose caller owns every buffer).  For callers that cannot call
+ * cudaMalloc when they run the block (an engine whose device memory comes from
+ * its own arena, a language binding with no device allocator, a step that must
+ * not touch the allocator): it needs no handle and no workspace.  Its scratch
+ * is a 1 MiB device array inside the library, held on every GPU that loads the
+ * library until exit.
+ *   - T in [1, 8]; larger T (or any bad argument) returns QF_ERR_ARG.
+ *   - Runs on the calling thread's current device, on `stream` (NULL: legacy
+ *     default stream).  The first call on a device resolves the array's device
+ *     address and kernel attributes; make it before any stream capture.
+ *   - All calls share the array: calls whose GPU work overlaps race.  Each
+ *     call clears what must start at zero (the status word); out-of-range
+ *     record ids are skipped on the device but not reported by this call.
+ *   - It allocates nothing (no cudaMalloc/cudaFree, no allocating library). */
+qf_status qf_moe_block_forward_static(int32_t scale_dtype, const qf_moe_layer *layer, int32_t T,
+                                      const uint16_t *x, const float *residual, float *out,
+                                      int32_t *idx_out, float *w_out, void *stream);
+
 /* ---- kernel timing (bench harness) ----------------------------------- */
 /* Records CUDA events around every launch of one kernel of the block
  * (0 router, 1 top-k/grouping, 2 gate/up, 3 down, 4 combine) issued on this

@@ -63,6 +63,8 @@ SIGNATURES = {
                                   C.POINTER(RoutingDesc), _P, _P, _P, C.c_size_t]),
     "qf_moe_stack_forward": (_S, [_P, C.POINTER(MoELayerDesc), _I, _I, _P, _P, _P, C.c_float,
                                   _P, _P, _P, C.c_size_t]),
+    "qf_moe_block_forward_static": (_S, [C.c_int32, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
+                                         _P, _P, _P]),
     "qf_moe_profile_begin": (_S, [_P, _I, _I]),
     "qf_moe_profile_end": (_S, [_P, C.POINTER(C.c_float), C.POINTER(_I)]),
     "qf_synth_records": (_S, [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _P,

@@ -202,6 +202,9 @@ def main():
         return float(t.item())
 
     def measure(T: int, steps: int, warmup: int, profile: bool, e2e: bool = False):
+        # T <= 8 runs one persistent kernel per step (the whole stack); larger T
+        # runs five kernels per block, of which k_gate_up streams the most bytes
+        prof_kernel = "fused" if T <= 8 else "gate_up"
         pool = torch.stack([Q.synth_hidden(1000 + rank, i * T, T) for i in range(POOL)])
         pool_dev = pool.to(dev)
         x_static = torch.empty((T, 2048), dtype=torch.float16, device=dev)
@@ -227,7 +230,7 @@ def main():
             Q.stack_forward(ctx, plan, x_static, out=out_static, workspace=ws)  # warm on stream
             torch.cuda.synchronize()
             if profile:
-                Q.profile_begin(ctx, "gate_up", 4 * args.layers)
+                Q.profile_begin(ctx, prof_kernel, 4 * args.layers)
             with torch.cuda.graph(g, stream=s):
                 Q.stack_forward(ctx, plan, x_static, out=out_static, workspace=ws)
         torch.cuda.synchronize()
@@ -272,14 +275,20 @@ def main():
             except Q.QfError:
                 # graph-captured timing nodes unavailable: time the same step eagerly
                 x_static.copy_(pool_dev[last])
-                Q.profile_begin(ctx, "gate_up", 4 * args.layers)
+                Q.profile_begin(ctx, prof_kernel, 4 * args.layers)
                 Q.stack_forward(ctx, plan, x_static, out=out_static, workspace=ws)
                 tot_ms, n = Q.profile_end(ctx)
-                res["gate_up_timing"] = "eager replay of the last timed step"
-            gu_bytes = float(np.mean((uniq[last] + 1) * GATE_UP_BYTES))
-            res["gate_up_ms"] = tot_ms / max(n, 1)
-            res["gate_up_launches"] = n
-            res["gate_up_bytes"] = gu_bytes
+                res["kernel_timing"] = "eager replay of the last timed step"
+            if prof_kernel == "fused":
+                kbytes = float(args.layers * (ROUTER_BYTES + COEF_BYTES + RECORD)
+                               + uniq[last].sum() * RECORD)
+            else:
+                kbytes = float(np.mean((uniq[last] + 1) * GATE_UP_BYTES))
+            res["kernel"] = "k_fused" if prof_kernel == "fused" else "k_gate_up"
+            res["kernel_ms"] = tot_ms / max(n, 1)
+            res["kernel_launches"] = n
+            res["kernel_bytes"] = kbytes
+            res["launches_per_step"] = 1 if prof_kernel == "fused" else 5 * args.layers
         del g
         return res
 
@@ -301,7 +310,7 @@ def main():
             cpu = {"value": rate, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                    "sample": f"{n} single tokens through one MoE block on the CPU oracle "
                              f"(~{args.cpu_seconds:.0f} s), extrapolated x{N_LAYERS} layers"}
-        achieved = head["gate_up_bytes"] / (head["gate_up_ms"] / 1e3) / 1e9
+        achieved = head["kernel_bytes"] / (head["kernel_ms"] / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -316,18 +325,18 @@ def main():
                        "parallelism": "replicas" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: each step streams ~%.0f MB of weights and "
                              "the input rotates over %d token batches" % (head["step_bytes"] / 1e6, POOL)},
-            "roofline": {"bound": "hbm", "kernel": "k_gate_up", "achieved": achieved,
+            "roofline": {"bound": "hbm", "kernel": head["kernel"], "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind, "traffic": None,
-                         "bytes_per_launch": head["gate_up_bytes"],
-                         "ms_per_launch": head["gate_up_ms"]},
+                         "bytes_per_launch": head["kernel_bytes"],
+                         "ms_per_launch": head["kernel_ms"]},
             "step_hbm": {"achieved": head["step_gbs"], "frac": head["step_gbs"] / hbm_peak,
                          "bytes_per_step": head["step_bytes"]},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e["tokens_per_s"], "unit": "tokens/s",
                     "h2d_bytes_per_step": args.batch * 2048 * 2,
                     "d2h_bytes_per_step": args.batch * 2048 * 4},
-            "gpu_launches": args.steps * args.layers * 5,
+            "gpu_launches": args.steps * head["launches_per_step"],
             "clocks": head["clocks"],
             "decode_batches": extras,
         }

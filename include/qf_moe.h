@@ -75,9 +75,9 @@ typedef struct qf_moe_dims {
  * (QwenQ4ActiveExpertStreamingRunner.swift:36-50) and the expert arena /
  * cache buffer (Q4BoundedExpertCache.swift:23). */
 typedef struct qf_moe_layer {
-    const uint8_t *router_w;   /* [experts * hidden] Q8 codes */
-    const uint16_t *router_s;  /* [experts * hidden/64] */
-    const uint16_t *router_b;
+    const uint8_t *router_w;   /* [experts * hidden] Q8 codes (16-byte aligned) */
+    const uint16_t *router_s;  /* [experts * hidden/64] (16-byte aligned) */
+    const uint16_t *router_b;  /* (16-byte aligned) */
     const uint8_t *coef_w;     /* [hidden] Q8 codes of the shared-expert gate */
     const uint16_t *coef_s;    /* [hidden/64] */
     const uint16_t *coef_b;
@@ -152,8 +152,9 @@ qf_status qf_moe_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
  *   x: fp16 [T * hidden] post-norm hidden; residual: fp32 [T * hidden] or NULL;
  *   out: fp32 [T * hidden]; idx_out/w_out: optional [T * top_k];
  *   routing: optional; workspace: >= qf_moe_workspace_size bytes (256-B aligned).
- * T in [1, 64] runs the decode kernels; larger T is rejected (QF_ERR_ARG)
- * until the prefill path is built. */
+ * T in [1, 8] runs one persistent cooperative kernel (all phases of the block,
+ * grid barriers between them); T in [9, 64] runs five kernels per block.
+ * Larger T is rejected (QF_ERR_ARG) until the prefill path is built. */
 qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
                                const uint16_t *x, const float *residual, float *out,
                                const qf_routing *routing, int32_t *idx_out, float *w_out,

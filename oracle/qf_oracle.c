@@ -456,26 +456,21 @@ void qfo_block(const qfo_layer *L, int T, const uint16_t *x, const float *residu
     (void)threads;
 }
 
-/* deltanet.metal:18-53 qwen_rmsnorm_f32 with a 64-thread group and unit weight:
- * thread i sums v*v over i, i+64, ... (fma chain), simd_sum per simdgroup,
- * simd_sum of the two partials, inv = 1/sqrt(mean+eps) (rsqrt restated as the
- * correctly rounded quotient), out = in*inv rounded to fp16 for the next block. */
+/* RMSNorm of the stack transition (deltanet.metal:18-53 qwen_rmsnorm_f32, unit
+ * weight): the reference sums v*v with an fma chain per thread and simd_sum,
+ * whose order Metal leaves open; the order fixed here (and used by the CUDA
+ * kernels) is 128 tiles of 16 consecutive elements, an fma chain inside each
+ * tile, tiles summed in order.  inv = 1/sqrt(mean + eps) is the correctly
+ * rounded form of the reference's rsqrt; out = fp16(in * inv). */
 void qfo_rmsnorm_to_f16(const float *in, int T, float eps, uint16_t *x_out) {
     for (int t = 0; t < T; t++) {
         const float *v = in + (size_t)t * QFO_HIDDEN;
-        float th[64];
-        for (int i = 0; i < 64; i++) {
+        float total = 0.0f;
+        for (int c = 0; c < QFO_HIDDEN / 16; c++) {
             float acc = 0.0f;
-            for (int j = i; j < QFO_HIDDEN; j += 64) acc = fmaf(v[j], v[j], acc);
-            th[i] = acc;
+            for (int j = 0; j < 16; j++) acc = fmaf(v[c * 16 + j], v[c * 16 + j], acc);
+            total = total + acc;
         }
-        float p[32];
-        float s0 = butterfly32(th);
-        float s1 = butterfly32(th + 32);
-        memset(p, 0, sizeof(p));
-        p[0] = s0;
-        p[1] = s1;
-        const float total = butterfly32(p);
         const float mean_sq = total / (float)QFO_HIDDEN;
         const float inv = 1.0f / sqrtf(mean_sq + eps);
         for (int i = 0; i < QFO_HIDDEN; i++)

@@ -120,7 +120,8 @@ void qfo_block(const qfo_layer *L, int T, const uint16_t *x, const float *residu
                const float *bias, const int32_t *idx_in, const float *w_in, float *out,
                int32_t *idx_out, float *w_out, float *logits_out, float *coef_out, int threads);
 
-/* RMSNorm of the stack transition, in the 64-thread order of deltanet.metal:18-53 */
+/* RMSNorm of the stack transition (deltanet.metal:18-53) in a fixed order: 128 tiles of
+ * 16 elements, fma chain per tile, tiles summed in order; out = fp16(in * inv) */
 void qfo_rmsnorm_to_f16(const float *in, int T, float eps, uint16_t *x_out);
 
 /* stable dispatch plan: counts[E], offsets[E+1], perm[T*k] sorted by (expert, token, k) */

@@ -4,6 +4,7 @@
 #include <string.h>
 
 #include <string>
+#include <vector>
 
 #include "../../include/qf_moe.h"
 #include "qf_internal.h"
@@ -66,9 +67,10 @@ qf_status layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
   if (l->record_stride < qf::kRecordBytes || (l->record_stride % 16) != 0)
     return fail(h, QF_ERR_ARG, "record_stride must be >= 1769472 and a multiple of 16");
   if (!aligned(l->router_w, 16) || !aligned(l->coef_w, 16) || !aligned(l->shared_record, 16) ||
-      !aligned(l->expert_bank, 16) || !aligned(l->router_s, 2) || !aligned(l->router_b, 2) ||
+      !aligned(l->expert_bank, 16) || !aligned(l->router_s, 16) || !aligned(l->router_b, 16) ||
       !aligned(l->coef_s, 2) || !aligned(l->coef_b, 2))
-    return fail(h, QF_ERR_ARG, "weight pointers must be 16-byte aligned (codes, records)");
+    return fail(h, QF_ERR_ARG,
+                "router codes/scales/biases, shared record and bank must be 16-byte aligned");
   if (l->bank_records == 0 || l->bank_records >= (1u << 23))
     return fail(h, QF_ERR_ARG, "bank_records must be in [1, 2^23)");
   if (l->reserved != 0) return fail(h, QF_ERR_ARG, "reserved field must be 0");
@@ -126,7 +128,8 @@ qf_status qf_moe_create(const qf_moe_dims* dims, int device, qf_moe** out) {
     delete h;
     return QF_ERR_OOM;
   }
-  if (cudaMemset(h->d_status, 0, 256) != cudaSuccess || qf::decode_init_attributes() != cudaSuccess) {
+  if (cudaMemset(h->d_status, 0, 256) != cudaSuccess || qf::decode_init_attributes() != cudaSuccess ||
+      qf::fused_init_attributes() != cudaSuccess) {
     cudaFree(h->d_status);
     delete h;
     return QF_ERR_CUDA;
@@ -220,7 +223,9 @@ qf_status qf_moe_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
   if (!h || !bytes) return QF_ERR_ARG;
   if (T < 1 || T > qf::kDecodeMaxTokens)
     return fail(h, QF_ERR_ARG, "T must be in [1, 64] for the decode path");
-  *bytes = qf::decode_workspace_bytes(T);
+  const size_t a = qf::decode_workspace_bytes(T);
+  const size_t b = T <= qf::kFusedMaxTokens ? qf::fused_workspace_bytes(T) : 0;
+  *bytes = a > b ? a : b;
   return QF_OK;
 }
 
@@ -235,17 +240,27 @@ qf_status qf_moe_block_forward(qf_moe* h, const qf_moe_layer* layer, int32_t T, 
   if (T < 1 || T > qf::kDecodeMaxTokens)
     return fail(h, QF_ERR_ARG, "T must be in [1, 64] (decode path)");
   if (!x || !out || !aligned(x, 16)) return fail(h, QF_ERR_ARG, "x (16-B aligned) and out are required");
-  if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::decode_workspace_bytes(T))
+  size_t need = 0;
+  qf_moe_workspace_size(h, T, &need);
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < need)
     return fail(h, QF_ERR_ARG, "workspace too small or not 256-byte aligned");
   qf::RoutingArgs r;
   s = routing_args(h, routing, &r);
   if (s != QF_OK) return s;
-  qf::DecodeWs ws;
-  qf::decode_carve(workspace, T, &ws);
   DeviceGuard g(h->device);
-  cudaError_t e = qf::decode_block(stream_of(h), w, h->dims.scale_dtype == QF_SCALE_BF16, T, x,
-                                   residual, out, r, idx_out, w_out, ws, nullptr, 0.f, h->d_status,
-                                   &h->prof);
+  const bool bf16 = h->dims.scale_dtype == QF_SCALE_BF16;
+  cudaError_t e;
+  if (T <= qf::kFusedMaxTokens && (h->prof.kernel < 0 || h->prof.kernel == qf::kKFused)) {
+    if (workspace_bytes < qf::fused_workspace_bytes(T))
+      return fail(h, QF_ERR_ARG, "workspace too small");
+    e = qf::fused_stack(stream_of(h), &w, 1, bf16, T, x, residual, out, 1e-6f, r, idx_out, w_out,
+                        workspace, h->d_status, &h->prof);
+  } else {
+    qf::DecodeWs ws;
+    qf::decode_carve(workspace, T, &ws);
+    e = qf::decode_block(stream_of(h), w, bf16, T, x, residual, out, r, idx_out, w_out, ws,
+                         nullptr, 0.f, h->d_status, &h->prof);
+  }
   return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_block_forward");
 }
 
@@ -261,22 +276,32 @@ qf_status qf_moe_stack_forward(qf_moe* h, const qf_moe_layer* layers, int32_t n_
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::decode_workspace_bytes(T))
     return fail(h, QF_ERR_ARG, "workspace too small or not 256-byte aligned");
   if (!(eps > 0.f)) return fail(h, QF_ERR_ARG, "eps must be > 0");
-  qf::DecodeWs ws;
-  qf::decode_carve(workspace, T, &ws);
+  size_t need = 0;
+  qf_moe_workspace_size(h, T, &need);
+  if (workspace_bytes < need) return fail(h, QF_ERR_ARG, "workspace too small");
+  std::vector<qf::LayerW> lw(n_layers);
+  for (int l = 0; l < n_layers; l++) {
+    qf_status s = layer_to_w(h, &layers[l], &lw[l]);
+    if (s != QF_OK) return s;
+  }
   qf::RoutingArgs r = {nullptr, nullptr, nullptr, nullptr};
   DeviceGuard g(h->device);
   const bool bf16 = h->dims.scale_dtype == QF_SCALE_BF16;
+  if (T <= qf::kFusedMaxTokens && (h->prof.kernel < 0 || h->prof.kernel == qf::kKFused)) {
+    cudaError_t e = qf::fused_stack(stream_of(h), lw.data(), n_layers, bf16, T, x, residual, out,
+                                    eps, r, idx_out, w_out, workspace, h->d_status, &h->prof);
+    return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_stack_forward");
+  }
+  qf::DecodeWs ws;
+  qf::decode_carve(workspace, T, &ws);
   const size_t PT = static_cast<size_t>(T) * qf::kTopK;
   for (int l = 0; l < n_layers; l++) {
-    qf::LayerW w;
-    qf_status s = layer_to_w(h, &layers[l], &w);
-    if (s != QF_OK) return s;
     const int cur = l & 1;
     const uint16_t* xin = (l == 0) ? x : ws.x16[cur];
     const float* res = (l == 0) ? residual : ws.h[cur];
     float* o = (l == n_layers - 1) ? out : ws.h[cur ^ 1];
     uint16_t* xn = (l == n_layers - 1) ? nullptr : ws.x16[cur ^ 1];
-    cudaError_t e = qf::decode_block(stream_of(h), w, bf16, T, xin, res, o, r,
+    cudaError_t e = qf::decode_block(stream_of(h), lw[l], bf16, T, xin, res, o, r,
                                      idx_out ? idx_out + l * PT : nullptr,
                                      w_out ? w_out + l * PT : nullptr, ws, xn, eps, h->d_status,
                                      &h->prof);
@@ -335,8 +360,8 @@ extern "C" {
 
 qf_status qf_moe_profile_begin(qf_moe* h, int32_t kernel_id, int32_t max_launches) {
   if (!h) return QF_ERR_ARG;
-  if (kernel_id < 0 || kernel_id > 4 || max_launches < 1 || max_launches > 65536)
-    return fail(h, QF_ERR_ARG, "kernel_id in [0,4], max_launches in [1,65536]");
+  if (kernel_id < 0 || kernel_id > 5 || max_launches < 1 || max_launches > 65536)
+    return fail(h, QF_ERR_ARG, "kernel_id in [0,5], max_launches in [1,65536]");
   DeviceGuard g(h->device);
   prof_release(&h->prof);
   h->prof.ev0 = new cudaEvent_t[max_launches];

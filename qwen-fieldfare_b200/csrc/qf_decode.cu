@@ -637,8 +637,7 @@ __global__ void __launch_bounds__(kThreads) k_combine(int T, const float* __rest
                                                       DecodeWs ws, float* __restrict__ out,
                                                       uint16_t* __restrict__ x_next, float eps) {
   __shared__ float o[kHidden];
-  __shared__ float part[2];
-  const int t = blockIdx.x;
+    const int t = blockIdx.x;
   const float c = ws.coef[t];
   const float coeff = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-c)));
   float w[kTopK];
@@ -657,16 +656,26 @@ __global__ void __launch_bounds__(kThreads) k_combine(int T, const float* __rest
   }
   if (x_next == nullptr) return;
   __syncthreads();
-  if (threadIdx.x < 64) {
+  // RMS over 128 tiles of 16 rows: fma chain inside a tile, tiles summed in order
+  __shared__ float tile_ss[kHidden / 16];
+  __shared__ float inv_s;
+  if (threadIdx.x < kHidden / 16) {
     float acc = 0.f;
-    for (int j = threadIdx.x; j < kHidden; j += 64) acc = __fmaf_rn(o[j], o[j], acc);
-    acc = warp_sum(acc);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    for (int j = 0; j < 16; j++) {
+      const float v = o[threadIdx.x * 16 + j];
+      acc = __fmaf_rn(v, v, acc);
+    }
+    tile_ss[threadIdx.x] = acc;
   }
   __syncthreads();
-  const float total = __fadd_rn(part[0], part[1]);
-  const float mean = __fdiv_rn(total, static_cast<float>(kHidden));
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  if (threadIdx.x == 0) {
+    float total = 0.f;
+    for (int c = 0; c < kHidden / 16; c++) total = __fadd_rn(total, tile_ss[c]);
+    const float mean = __fdiv_rn(total, static_cast<float>(kHidden));
+    inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  __syncthreads();
+  const float inv = inv_s;
   for (int r = threadIdx.x; r < kHidden; r += kThreads)
     x_next[static_cast<size_t>(t) * kHidden + r] = __half_as_ushort(__float2half_rn(__fmul_rn(o[r], inv)));
 }

@@ -1,0 +1,1062 @@
+// qf_fused.cu -- persistent decode kernel for T <= 8 tokens and any number of
+// stacked MoE blocks: one cooperative launch runs the whole stack.
+//
+// Per layer, three phases separated by grid barriers (bounded spins):
+//   R  shared-expert gate/up (tensor cores) + router logits in the reference
+//      lane order (CUDA cores, bit-reproducible) + shared-gate coefficient
+//   E  top-k (every CTA, redundantly, warp redux) + grouping of positions by
+//      bank record; routed gate/up + shared down; L2 bulk prefetch of the
+//      routed experts' down projections
+//   D  routed down + combine in router order (deltanet.metal:2213-2227) +
+//      RMSNorm partials for the next block; L2 bulk prefetch of the next
+//      layer's router and shared expert
+// Weights move HBM/L2 -> shared memory through a ring of stages filled by
+// asynchronous 16-byte copies (cp.async, completion counted on one mbarrier per
+// stage), issued several tasks ahead of the warps that consume them, so each SM
+// keeps >100 KB in flight; rows land at a padded pitch so that the MMA
+// fragment reads are free of bank conflicts.
+//
+// Q4 dequant is exact: a LOP3 puts two nibbles into fp16 halves as 1024+q (or
+// 1024+16q for the odd elements, whose activation is fed as x/16), mma.sync
+// m16n8k16 multiplies by fp16 activations with fp32 accumulation, and the
+// constant is removed per 64-column group before the group scale:
+//   sum_e (q_e s + b) x_e = s (D - C) + b S,  D = MMA sum, C = 1024*sum(fed x), S = sum(x).
+// The A operand comes from registers: tcgen05 would need the dequantised
+// weights in shared memory or TMEM, i.e. 4 bytes of on-chip traffic per
+// weight against 0.5 byte from HBM.
+#include <math.h>
+
+#include "qf_internal.h"
+
+namespace qf {
+
+namespace {
+
+constexpr int kFThreads = 512;
+constexpr int kFWarps = kFThreads / 32;
+constexpr int kFMaxT = 8;
+constexpr int kFMaxPos = kFMaxT * kTopK;  // 64
+constexpr int kOutTiles = kHidden / 16;   // 128 output tiles of 16 rows
+constexpr unsigned kSpinLimit = 1u << 22;  // bounded waits: a few seconds at most
+constexpr int kStatusTimeout = -6;
+
+// ---- stage layouts (bytes) ----
+constexpr int kGuPitch = 1024 + 32;                  // padded gate/up row
+constexpr int kGuStage = 32 * kGuPitch + 4 * 1024;   // 16 rows x (gate, up) + s/b
+constexpr int kDnPitch = 256 + 32;                   // padded down row
+constexpr int kDnGroupBytes = 16 * kDnPitch + 2 * 16 * 16;  // 16 rows + s/b (5120)
+constexpr int kDnGroupsPerStage = 8;
+constexpr int kShDnRows = 64;
+constexpr int kShDnStage = kShDnRows * kDnPitch + 2 * kShDnRows * 16;  // 20480
+constexpr int kRtStage = 16 * 2048 + 2 * 16 * 64;    // 16 router rows + s/b (34816)
+constexpr int kStageBytes = kDnGroupsPerStage * kDnGroupBytes;  // largest stage (40960)
+static_assert(kGuStage <= kStageBytes, "stage");
+static_assert(kRtStage <= kStageBytes && kShDnStage <= kStageBytes, "stage");
+
+// ---- shared memory layout, sized by T (offsets in bytes) ----
+//   U      union: fp16 x [T][2048] (phase R)  |  act fragments [8][8T][4][32 B] (phase D)
+//   xfrag  x fragments [32][T][4][32 B]
+//   shfrag shared-expert act fragments [8][T][4][32 B]
+//   fixed  S/C arrays, reduction buffer, small state, mbarriers
+//   ring   stages of kStageBytes
+constexpr int kSmMax = 227 * 1024;
+constexpr int kMaxStages = 5;
+struct SmLayout {
+  int u, xfrag, shfrag, xS, xC, shS, shC, aS, aC, red, misc, bar, ring, nstages, total;
+};
+__host__ __device__ inline SmLayout sm_layout(int T) {
+  SmLayout L;
+  L.u = 0;
+  L.xfrag = L.u + 8 * T * 1024;
+  L.shfrag = L.xfrag + 4 * T * 1024;
+  L.xS = L.shfrag + T * 1024;
+  L.xC = L.xS + 1024;
+  L.shS = L.xC + 1024;
+  L.shC = L.shS + 256;
+  L.aS = L.shC + 256;
+  L.aC = L.aS + 2048;
+  L.red = L.aC + 2048;
+  L.misc = L.red + 8192;
+  L.bar = L.misc + 4096;
+  L.ring = (L.bar + 64 + 127) & ~127;
+  int n = (kSmMax - L.ring) / kStageBytes;
+  L.nstages = n > kMaxStages ? kMaxStages : n;
+  L.total = L.ring + L.nstages * kStageBytes;
+  return L;
+}
+
+struct Misc {
+  int idx[kFMaxPos];
+  float w[kFMaxPos];
+  int ng;
+  int grp_rec[kFMaxPos];     // record of group g
+  int grp_start[kFMaxPos];   // first index into sorted_pos
+  int grp_cnt[kFMaxPos];
+  int sorted_pos[kFMaxPos];  // positions t*8+k sorted by (record, position)
+  int rec_pos[kFMaxPos];     // record of position p
+  int skey[kFMaxPos];        // sorted (record << 6 | position)
+  float inv[kFMaxT];
+  int cols[8];
+  int fail;
+};
+static_assert(sizeof(Misc) <= 4096, "misc");
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// bounded wait for the phase with the given parity to complete
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (unsigned spins = 0; spins < kSpinLimit; spins++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+// 16-byte async copy global -> shared (L2 only), and the arrive that fires on
+// `bar` once every cp.async issued so far by this thread has landed.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bulk L2 prefetch; needs a 16-byte aligned address and a multiple-of-16 size.
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0 || (bytes & 15u) != 0) return;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier: one monotonically increasing arrival counter (zeroed before the
+// launch); arrival is a release reduction, the wait an acquire poll.  Bounded:
+// on expiry the status word gets QF_ERR_TIMEOUT and the CTA leaves the kernel
+// (the others then expire too).
+__device__ __forceinline__ bool grid_sync(unsigned* count, unsigned& epoch, int* status, Misc* m) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    epoch++;
+    red_release_add(count, 1u);
+    const unsigned target = gridDim.x * epoch;
+    unsigned spins = 0;
+    while (ld_acquire(count) < target) {
+      if (++spins > kSpinLimit) {
+        set_status(status, kStatusTimeout);
+        m->fail = 1;
+        break;
+      }
+      if (spins > 64) __nanosleep(20);
+    }
+  }
+  __syncthreads();
+  return m->fail == 0;
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// two nibbles of a word as fp16 halves 1024+q (j even) or 1024+16q (j odd)
+__device__ __forceinline__ uint32_t pairsel(uint32_t w, int j) {
+  const uint32_t v = (j >= 2) ? (w >> 8) : w;
+  const uint32_t mask = (j & 1) ? 0x00F000F0u : 0x000F000Fu;
+  return (v & mask) | 0x64006400u;
+}
+
+// Half index of element e (0..63 of a 64-column group) inside the 32-byte
+// fragment chunk of its thread-slot t = e/16.
+__device__ __forceinline__ int frag_half(int e) {
+  const int w2 = (e & 15) >> 3, k = e & 7, j = k & 3, hi = k >> 2;
+  return (j * 2 + w2) * 2 + hi;
+}
+
+// Stage nvec activation vectors (ngrp groups of 64 values each) as MMA B
+// fragments: item = (vector, group, eighth); each thread handles 8 values
+// (two float4 loads, all issued before any use), 8 consecutive lanes reduce S
+// and C for their group.  Vector v goes to fragment column v.
+template <bool kHalfSrc>
+__device__ __forceinline__ void stage_block(const void* src, int nvec, int ngrp, size_t vec_stride,
+                                            int ncols, __half* frag, float* S, float* C) {
+  const int items = nvec * ngrp * 8;
+  for (int base = 0; base < items; base += 2 * kFThreads) {
+    float vals[2][8];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int item = base + u * kFThreads + threadIdx.x;
+      if (item < items) {
+        const int v = item / (ngrp * 8), g = (item >> 3) % ngrp, q = item & 7;
+        const size_t off = v * vec_stride + g * 64 + q * 8;
+        if constexpr (kHalfSrc) {
+          const uint4 hv = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(src) + off);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&hv);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const float2 f = __half22float2(h2[j]);
+            vals[u][2 * j] = f.x;
+            vals[u][2 * j + 1] = f.y;
+          }
+        } else {
+          const float4 a = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + off));
+          const float4 b = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + off + 4));
+          vals[u][0] = a.x; vals[u][1] = a.y; vals[u][2] = a.z; vals[u][3] = a.w;
+          vals[u][4] = b.x; vals[u][5] = b.y; vals[u][6] = b.z; vals[u][7] = b.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int item0 = base + u * kFThreads;
+      if (item0 >= items) break;  // uniform across the CTA
+      const int item = item0 + threadIdx.x;
+      float s_part = 0.f, c_part = 0.f;
+      int v = 0, g = 0;
+      if (item < items) {
+        v = item / (ngrp * 8);
+        g = (item >> 3) % ngrp;
+        const int q = item & 7;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int e = q * 8 + j;
+          const __half xh = __float2half_rn(vals[u][j]);
+          const __half fed = (e & 1) ? __float2half_rn(__half2float(xh) * 0.0625f) : xh;
+          frag[(((size_t)g * ncols + v) * 4 + (e >> 4)) * 16 + frag_half(e)] = fed;
+          s_part += __half2float(xh);
+          c_part += __half2float(fed);
+        }
+      }
+#pragma unroll
+      for (int mm = 1; mm < 8; mm <<= 1) {
+        s_part += __shfl_xor_sync(0xffffffffu, s_part, mm);
+        c_part += __shfl_xor_sync(0xffffffffu, c_part, mm);
+      }
+      if (item < items && (item & 7) == 0) {
+        S[g * ncols + v] = s_part;
+        C[g * ncols + v] = 1024.f * c_part;
+      }
+    }
+  }
+}
+
+// One warp: a 16-row tile x NG groups (starting at grp0) of a Q4 matrix held in
+// shared memory (rows at `pitch` bytes; scales/biases s, b as [16][sgroups]
+// halves), against up to 8 activation columns (cols[s] = fragment column of
+// slot s, or -1).  acc: rows (g, g+8) x slots (2t, 2t+1).
+template <bool BF16, int NG>
+__device__ __forceinline__ void mma_tile_smem(const uint8_t* rows, int pitch, int grp0,
+                                              const uint16_t* s, const uint16_t* b, int sgroups,
+                                              const __half* frag, const float* S, const float* C,
+                                              int ncols, const int* cols, float (&acc)[4],
+                                              int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const int colb = cols[g];
+  const int c0 = cols[2 * t], c1 = cols[2 * t + 1];
+#pragma unroll
+  for (int i = 0; i < NG; i++) {
+    const int grp = grp0 + i;
+    const uint2 wa = *reinterpret_cast<const uint2*>(rows + g * pitch + grp * 32 + 8 * t);
+    const uint2 wb = *reinterpret_cast<const uint2*>(rows + (g + 8) * pitch + grp * 32 + 8 * t);
+    float sa, ba, sb, bb;
+    if constexpr (BF16) {
+      sa = __uint_as_float((uint32_t)s[g * sgroups + grp] << 16);
+      ba = __uint_as_float((uint32_t)b[g * sgroups + grp] << 16);
+      sb = __uint_as_float((uint32_t)s[(g + 8) * sgroups + grp] << 16);
+      bb = __uint_as_float((uint32_t)b[(g + 8) * sgroups + grp] << 16);
+    } else {
+      sa = __half2float(__ushort_as_half(s[g * sgroups + grp]));
+      ba = __half2float(__ushort_as_half(b[g * sgroups + grp]));
+      sb = __half2float(__ushort_as_half(s[(g + 8) * sgroups + grp]));
+      bb = __half2float(__ushort_as_half(b[(g + 8) * sgroups + grp]));
+    }
+    uint4 bf0 = make_uint4(0, 0, 0, 0), bf1 = make_uint4(0, 0, 0, 0);
+    if (colb >= 0) {
+      const uint4* p = reinterpret_cast<const uint4*>(frag + (((size_t)grp * ncols + colb) * 4 + t) * 16);
+      bf0 = p[0];
+      bf1 = p[1];
+    }
+    const uint32_t bw[8] = {bf0.x, bf0.y, bf0.z, bf0.w, bf1.x, bf1.y, bf1.z, bf1.w};
+    float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint32_t a[4];
+      a[0] = pairsel(wa.x, j);
+      a[1] = pairsel(wb.x, j);
+      a[2] = pairsel(wa.y, j);
+      a[3] = pairsel(wb.y, j);
+      mma16816(tmp, a, bw[2 * j], bw[2 * j + 1]);
+    }
+    const float S0 = c0 >= 0 ? S[grp * ncols + c0] : 0.f;
+    const float C0 = c0 >= 0 ? C[grp * ncols + c0] : 0.f;
+    const float S1 = c1 >= 0 ? S[grp * ncols + c1] : 0.f;
+    const float C1 = c1 >= 0 ? C[grp * ncols + c1] : 0.f;
+    acc[0] = __fmaf_rn(sa, tmp[0] - C0, __fmaf_rn(ba, S0, acc[0]));
+    acc[1] = __fmaf_rn(sa, tmp[1] - C1, __fmaf_rn(ba, S1, acc[1]));
+    acc[2] = __fmaf_rn(sb, tmp[2] - C0, __fmaf_rn(bb, S0, acc[2]));
+    acc[3] = __fmaf_rn(sb, tmp[3] - C1, __fmaf_rn(bb, S1, acc[3]));
+  }
+}
+
+constexpr int kFMaxLayers = 64;
+
+struct FusedArgs {
+  int T;
+  int n_layers;      // layers in this launch
+  int first_layer;   // global index of layer 0 of this launch
+  int total_layers;  // layers of the whole stack
+  const uint16_t* x0;
+  const float* res0;
+  float* out;
+  float eps;
+  RoutingArgs r;
+  int* idx_out;
+  float* w_out;
+  float* logits;
+  float* coef;
+  float* act;
+  float* act_sh;
+  float* y_sh;
+  float* h0;
+  float* h1;
+  float* ssq;
+  unsigned* bar;
+  int* status;
+  LayerW layers[kFMaxLayers];
+};
+
+enum TaskKind { kRouterTask = 0, kSharedGuTask = 1, kGuTask = 2, kShDnTask = 3, kDnTask = 4 };
+
+// Copy `rows` rows of `row_bytes` (multiple of 16) from src (rows at src_pitch)
+// into shared memory at dst_pitch, 16 bytes per cp.async, spread over the CTA.
+__device__ __forceinline__ void copy_rows(unsigned char* dst, int dst_pitch, const uint8_t* src,
+                                          size_t src_pitch, int rows, int row_bytes) {
+  const int per_row = row_bytes >> 4;
+  for (int c = threadIdx.x; c < rows * per_row; c += blockDim.x) {
+    const int r = c / per_row, q = c - r * per_row;
+    cp_async16(dst + r * dst_pitch + q * 16, src + r * src_pitch + q * 16);
+  }
+}
+
+// Issue the copies of one task into `stage`; every thread of the CTA takes part
+// and then arrives on the stage's mbarrier (init count = threads per CTA), so
+// the barrier completes once all copies have landed.
+__device__ void issue_task(const LayerW& L, const Misc* m, int kind, int a, int b,
+                           unsigned char* stage, uint64_t* full) {
+  if (kind == kRouterTask) {
+    // 16 router rows (rows >= 256 skipped) + their scales/biases
+    const int r0 = a * 16;
+    const int nr = r0 + 16 <= kExperts ? 16 : (r0 < kExperts ? kExperts - r0 : 0);
+    if (nr > 0) {
+      copy_rows(stage, 2048, L.rw + (size_t)r0 * 2048, 2048, nr, 2048);
+      copy_rows(stage + 16 * 2048, 64, reinterpret_cast<const uint8_t*>(L.rs + r0 * 32), 64, nr, 64);
+      copy_rows(stage + 16 * 2048 + 1024, 64, reinterpret_cast<const uint8_t*>(L.rb + r0 * 32), 64, nr, 64);
+    }
+  } else if (kind == kSharedGuTask || kind == kGuTask) {
+    const uint8_t* rec = (kind == kSharedGuTask) ? L.shared : L.bank + (uint64_t)m->grp_rec[b] * L.stride;
+    const int r0 = a * 16;
+    copy_rows(stage, kGuPitch, rec + kOffGateW + (size_t)r0 * 1024, 1024, 16, 1024);
+    copy_rows(stage + 16 * kGuPitch, kGuPitch, rec + kOffUpW + (size_t)r0 * 1024, 1024, 16, 1024);
+    unsigned char* sb = stage + 32 * kGuPitch;
+    copy_rows(sb, 1024, rec + kOffGateS + (size_t)r0 * 64, 1024, 1, 1024);
+    copy_rows(sb + 1024, 1024, rec + kOffGateB + (size_t)r0 * 64, 1024, 1, 1024);
+    copy_rows(sb + 2048, 1024, rec + kOffUpS + (size_t)r0 * 64, 1024, 1, 1024);
+    copy_rows(sb + 3072, 1024, rec + kOffUpB + (size_t)r0 * 64, 1024, 1, 1024);
+  } else if (kind == kShDnTask) {
+    const int r0 = a * kShDnRows;
+    copy_rows(stage, kDnPitch, L.shared + kOffDownW + (size_t)r0 * 256, 256, kShDnRows, 256);
+    unsigned char* sb = stage + kShDnRows * kDnPitch;
+    copy_rows(sb, kShDnRows * 16, L.shared + kOffDownS + (size_t)r0 * 16, 0, 1, kShDnRows * 16);
+    copy_rows(sb + kShDnRows * 16, kShDnRows * 16, L.shared + kOffDownB + (size_t)r0 * 16, 0, 1,
+              kShDnRows * 16);
+  } else {
+    // kDnTask: output tile a, groups [b, b + 8) of the routed down projections
+    const int r0 = a * 16;
+    const int g1 = b + kDnGroupsPerStage < m->ng ? b + kDnGroupsPerStage : m->ng;
+    for (int gi = b; gi < g1; gi++) {
+      const uint8_t* rec = L.bank + (uint64_t)m->grp_rec[gi] * L.stride;
+      unsigned char* gs = stage + (gi - b) * kDnGroupBytes;
+      copy_rows(gs, kDnPitch, rec + kOffDownW + (size_t)r0 * 256, 256, 16, 256);
+      copy_rows(gs + 16 * kDnPitch, 256, rec + kOffDownS + (size_t)r0 * 16, 0, 1, 256);
+      copy_rows(gs + 16 * kDnPitch + 256, 256, rec + kOffDownB + (size_t)r0 * 16, 0, 1, 256);
+    }
+  }
+  cp_async_arrive(full);
+}
+
+// ----- router rows of one task from the stage (reference lane order) -----
+template <bool BF16>
+__device__ void router_task(const FusedArgs& A, const LayerW& L, const unsigned char* stage,
+                            const __half* xh, int task, int warp, int lane) {
+  const int T = A.T;
+  const int row = task * 16 + warp;
+  if (row < kExperts) {
+    const uint8_t* wrow = stage + warp * 2048;
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(stage + 16 * 2048) + warp * 32;
+    const uint16_t* brow = reinterpret_cast<const uint16_t*>(stage + 16 * 2048 + 1024) + warp * 32;
+    uint2 wv[8];
+    float sc[8], bi[8];
+#pragma unroll
+    for (int blk = 0; blk < 8; blk++) {
+      wv[blk] = *reinterpret_cast<const uint2*>(wrow + blk * 256 + lane * 8);
+      const int gq = blk * 4 + (lane >> 3);
+      if constexpr (BF16) {
+        sc[blk] = __uint_as_float((uint32_t)srow[gq] << 16);
+        bi[blk] = __uint_as_float((uint32_t)brow[gq] << 16);
+      } else {
+        sc[blk] = __half2float(__ushort_as_half(srow[gq]));
+        bi[blk] = __half2float(__ushort_as_half(brow[gq]));
+      }
+    }
+    for (int t = 0; t < T; t++) {
+      float acc = 0.f;
+#pragma unroll
+      for (int blk = 0; blk < 8; blk++) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(xh + t * kHidden + blk * 256 + lane * 8);
+        const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&hv.x));
+        const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&hv.y));
+        const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&hv.z));
+        const float2 p3 = __half22float2(*reinterpret_cast<const __half2*>(&hv.w));
+        const float e[8] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y, p3.x, p3.y};
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dot = __fmaf_rn(byte_f(wv[blk].x, i), e[i], dot);
+#pragma unroll
+        for (int i = 0; i < 4; i++) dot = __fmaf_rn(byte_f(wv[blk].y, i), e[4 + i], dot);
+        float sum = e[0];
+#pragma unroll
+        for (int i = 1; i < 8; i++) sum = __fadd_rn(sum, e[i]);
+        acc = __fmaf_rn(sc[blk], dot, acc);
+        acc = __fmaf_rn(bi[blk], sum, acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) A.logits[t * kExperts + row] = acc;
+    }
+  } else if (row == kExperts) {
+    // shared-gate coefficient (Q8, one row), read straight from global
+    const float cs = ld16<BF16>(L.cs, lane), cb = ld16<BF16>(L.cb, lane);
+    uint4 cwv[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) cwv[q] = __ldg(reinterpret_cast<const uint4*>(L.cw + lane * 64) + q);
+    for (int t = 0; t < T; t++) {
+      float acc = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+#pragma unroll
+        for (int d = 0; d < 4; d++) {
+          const uint32_t wd = word_of(cwv[q], d);
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float xe = __half2float(xh[t * kHidden + lane * 64 + q * 16 + d * 4 + k]);
+            acc = __fmaf_rn(__fmaf_rn(byte_f(wd, k), cs, cb), xe, acc);
+          }
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) A.coef[t] = acc;
+    }
+  }
+}
+
+// Gate/up task from the stage: 16 rows of G and U, K = 2048, warps = 2 matrices
+// x 8 K-eighths; the first 128 threads reduce and apply SiLU * up.
+template <bool BF16>
+__device__ void gu_task(const unsigned char* stage, const __half* xfrag, const float* xS,
+                        const float* xC, int ncols, const int* cols, int row0, float* red, int warp,
+                        int lane, float* dst, const int* dst_row_of_slot, int nslots) {
+  const int mat = warp >> 3, kq = warp & 7;
+  const uint8_t* rows = stage + mat * 16 * kGuPitch;
+  const uint16_t* s = reinterpret_cast<const uint16_t*>(stage + 32 * kGuPitch + mat * 2048);
+  const uint16_t* b = reinterpret_cast<const uint16_t*>(stage + 32 * kGuPitch + mat * 2048 + 1024);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_tile_smem<BF16, 4>(rows, kGuPitch, kq * 4, s, b, 32, xfrag, xS, xC, ncols, cols, acc, lane);
+  const int g = lane >> 2, t = lane & 3;
+  float* r = red + warp * 128;  // [16 rows][8 slots]
+  r[g * 8 + 2 * t] = acc[0];
+  r[g * 8 + 2 * t + 1] = acc[1];
+  r[(g + 8) * 8 + 2 * t] = acc[2];
+  r[(g + 8) * 8 + 2 * t + 1] = acc[3];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int row = threadIdx.x >> 3, slot = threadIdx.x & 7;
+    if (slot < nslots) {
+      float gs = 0.f, us = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        gs = __fadd_rn(gs, red[q * 128 + row * 8 + slot]);
+        us = __fadd_rn(us, red[(8 + q) * 128 + row * 8 + slot]);
+      }
+      dst[(size_t)dst_row_of_slot[slot] * kInter + row0 + row] = silu_mul(gs, us);
+    }
+  }
+}
+
+// top-k of token `t` by one warp: 8 rounds of (max value, then min index among
+// the lanes holding it) with warp reductions; orders ties like the reference's
+// strict-> insertion scan (deltanet.metal:2283-2329).
+__device__ __forceinline__ uint32_t f2ord(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+__device__ void topk_warp(const float* logits, const float* bias, int t, int lane, int* idx_out,
+                          float* w_out) {
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = j * 32 + lane;
+    const float lg = __ldcg(logits + t * kExperts + e);
+    v[j] = bias ? __fadd_rn(lg, __ldg(bias + e)) : lg;
+  }
+  unsigned taken = 0;
+  float selv[kTopK];
+  int seli[kTopK];
+#pragma unroll
+  for (int k = 0; k < kTopK; k++) {
+    uint32_t best = 0;
+    int bj = 0;
+#pragma unroll
+    for (int j = 7; j >= 0; j--) {  // ties within a lane: lower j (lower expert id) wins
+      const uint32_t o = ((taken >> j) & 1u) ? 0u : f2ord(v[j]);
+      if (o >= best) {
+        best = o;
+        bj = j;
+      }
+    }
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t cand = (best == mx) ? (uint32_t)(bj * 32 + lane) : 0xffffffffu;
+    const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
+    if ((int)(win & 31) == lane) taken |= 1u << (win >> 5);
+    selv[k] = ord2f(mx);
+    seli[k] = (int)win;
+  }
+  const float mxv = selv[0];
+  float den = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; j++) den = __fadd_rn(den, expf(__fsub_rn(v[j], mxv)));
+  den = warp_sum(den);
+  float p[kTopK];
+  float ps = 0.f;
+#pragma unroll
+  for (int k = 0; k < kTopK; k++) {
+    p[k] = __fdiv_rn(expf(__fsub_rn(selv[k], mxv)), den);
+    ps = __fadd_rn(ps, p[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < kTopK; k++)
+    if (lane == k) {
+      idx_out[t * kTopK + k] = seli[k];
+      w_out[t * kTopK + k] = __fdiv_rn(p[k], ps);
+    }
+}
+
+// Task lists of the three phases by CTA-local index i.  R and E deal tasks
+// round-robin (task = blockIdx.x + i * gridDim.x); D gives each CTA whole
+// output tiles (tile = blockIdx.x + (i / nchunk) * gridDim.x, all its group
+// chunks in a row) because a tile's combine reads every chunk's result.
+struct PhaseR {
+  __device__ int task(int i) const { return (int)blockIdx.x + i * (int)gridDim.x; }
+  __device__ void operator()(int i, int& kind, int& a, int& b) const {
+    const int t = task(i);
+    kind = t < 32 ? kSharedGuTask : kRouterTask;
+    a = t < 32 ? t : t - 32;
+    b = 0;
+  }
+};
+struct PhaseE {
+  int n_gu;
+  __device__ int task(int i) const { return (int)blockIdx.x + i * (int)gridDim.x; }
+  __device__ void operator()(int i, int& kind, int& a, int& b) const {
+    const int task = this->task(i);
+    if (task < n_gu) {
+      kind = kGuTask;
+      a = task & 31;
+      b = task >> 5;
+    } else {
+      kind = kShDnTask;
+      a = task - n_gu;
+      b = 0;
+    }
+  }
+};
+struct PhaseD {
+  int nchunk;
+  __device__ int tile(int i) const { return (int)blockIdx.x + (i / nchunk) * (int)gridDim.x; }
+  __device__ void operator()(int i, int& kind, int& a, int& b) const {
+    kind = kDnTask;
+    a = tile(i);
+    b = (i % nchunk) * kDnGroupsPerStage;
+  }
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(kFThreads, 1) k_fused(const __grid_constant__ FusedArgs A) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  const int T = A.T;
+  const SmLayout SL = sm_layout(T);
+  __half* xh = reinterpret_cast<__half*>(sm + SL.u);     // phase R
+  __half* afrag = reinterpret_cast<__half*>(sm + SL.u);  // phase D (same bytes)
+  __half* xfrag = reinterpret_cast<__half*>(sm + SL.xfrag);
+  __half* shfrag = reinterpret_cast<__half*>(sm + SL.shfrag);
+  float* xS = reinterpret_cast<float*>(sm + SL.xS);
+  float* xC = reinterpret_cast<float*>(sm + SL.xC);
+  float* shS = reinterpret_cast<float*>(sm + SL.shS);
+  float* shC = reinterpret_cast<float*>(sm + SL.shC);
+  float* aS = reinterpret_cast<float*>(sm + SL.aS);
+  float* aC = reinterpret_cast<float*>(sm + SL.aC);
+  float* red = reinterpret_cast<float*>(sm + SL.red);
+  Misc* m = reinterpret_cast<Misc*>(sm + SL.misc);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + SL.bar);
+  unsigned char* ring = sm + SL.ring;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int npos = T * kTopK;
+  const int G = gridDim.x;
+  const int NS = SL.nstages;
+  unsigned epoch = 0;
+  uint32_t uses[kMaxStages];
+#pragma unroll
+  for (int i = 0; i < kMaxStages; i++) uses[i] = 0;
+  if (tid == 0) {
+    for (int i = 0; i < NS; i++) mbar_init(&full[i], kFThreads);
+    m->fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // Issue the first NS tasks of a phase into the ring (thread 0).
+  auto prime = [&](const LayerW& L, int n_my, auto describe) {
+    for (int i = 0; i < n_my && i < NS; i++) {
+      int kind, ta, tb;
+      describe(i, kind, ta, tb);
+      issue_task(L, m, kind, ta, tb, ring + (size_t)i * kStageBytes, &full[i]);
+    }
+  };
+  // Wait for task i's stage; returns the stage (nullptr after a timeout).
+  auto acquire = [&](int i) -> unsigned char* {
+    const int st = i % NS;
+    if (!mbar_wait(&full[st], uses[st] & 1u)) {
+      set_status(A.status, kStatusTimeout);
+      m->fail = 1;
+    }
+    uses[st]++;
+    return ring + (size_t)st * kStageBytes;
+  };
+  // After the task's closing __syncthreads: refill its stage with task i + NS.
+  auto release = [&](const LayerW& L, int i, int n_my, auto describe) {
+    if (i + NS < n_my) {
+      const int st = i % NS;
+      int kind, ta, tb;
+      describe(i + NS, kind, ta, tb);
+      issue_task(L, m, kind, ta, tb, ring + (size_t)st * kStageBytes, &full[st]);
+    }
+  };
+  auto n_mine = [&](int ntasks) { return ntasks > (int)blockIdx.x ? (ntasks - 1 - (int)blockIdx.x) / G + 1 : 0; };
+
+  for (int li = 0; li < A.n_layers; li++) {
+    const int l = A.first_layer + li;  // global layer index (ping-pong parity)
+    const LayerW& L = A.layers[li];
+    const float* res = (l == 0) ? A.res0 : ((l & 1) ? A.h1 : A.h0);
+    const float* hin = (l & 1) ? A.h1 : A.h0;
+    float* o = (l == A.total_layers - 1) ? A.out : ((l & 1) ? A.h0 : A.h1);
+
+    // phase R weights do not depend on x: issue them before the prologue
+    const PhaseR dR;
+    const int nR_my = n_mine(32 + 17);
+    prime(L, nR_my, dR);
+
+    // ---------------- prologue: this layer's x (fp16) and its MMA fragments
+    // x_0 is the input; x_l = fp16(h_l / rms(h_l)), the RMS summed over 128 row
+    // tiles of 16 rows (fma chain inside a tile, tiles summed in order).
+    if (l == 0) {
+      for (int i = tid; i < T * kHidden / 8; i += kFThreads)
+        reinterpret_cast<uint4*>(xh)[i] = reinterpret_cast<const uint4*>(A.x0)[i];
+    } else {
+      // issue the loads first (h rows, four float4 per thread per pass, and the
+      // 128 tile partials per token), then normalise
+      constexpr int kPass = 4;
+      float4 hv[kPass];
+#pragma unroll
+      for (int u = 0; u < kPass; u++) {
+        const int i = u * kFThreads + tid;
+        if (i < T * kHidden / 4) hv[u] = __ldcg(reinterpret_cast<const float4*>(hin) + i);
+      }
+      if (tid < T * kOutTiles) red[tid] = __ldcg(A.ssq + (tid % kOutTiles) * kFMaxT + tid / kOutTiles);
+      __syncthreads();
+      if (tid < T) {
+        float tot = 0.f;
+        for (int c = 0; c < kOutTiles; c++) tot = __fadd_rn(tot, red[tid * kOutTiles + c]);
+        const float mean = __fdiv_rn(tot, (float)kHidden);
+        m->inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, A.eps)));
+      }
+      __syncthreads();
+      for (int pass = 0; pass * kPass * kFThreads < T * kHidden / 4; pass++) {
+        if (pass > 0) {
+#pragma unroll
+          for (int u = 0; u < kPass; u++) {
+            const int i = (pass * kPass + u) * kFThreads + tid;
+            if (i < T * kHidden / 4) hv[u] = __ldcg(reinterpret_cast<const float4*>(hin) + i);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kPass; u++) {
+          const int i = (pass * kPass + u) * kFThreads + tid;
+          if (i < T * kHidden / 4) {
+            const float iv = m->inv[(4 * i) / kHidden];
+            reinterpret_cast<__half2*>(xh)[2 * i] = __halves2half2(
+                __float2half_rn(__fmul_rn(hv[u].x, iv)), __float2half_rn(__fmul_rn(hv[u].y, iv)));
+            reinterpret_cast<__half2*>(xh)[2 * i + 1] = __halves2half2(
+                __float2half_rn(__fmul_rn(hv[u].z, iv)), __float2half_rn(__fmul_rn(hv[u].w, iv)));
+          }
+        }
+      }
+    }
+    __syncthreads();
+    stage_block<true>(xh, T, 32, kHidden, T, xfrag, xS, xC);
+    if (tid < 8) m->cols[tid] = tid < T ? tid : -1;
+    __syncthreads();
+
+    // ---------------- phase R: 32 shared gate/up tiles + 17 router tasks
+    for (int i = 0; i < nR_my; i++) {
+      const int task = dR.task(i);
+      unsigned char* stage = acquire(i);
+      if (task < 32) {
+        int rows_of_slot[8];
+#pragma unroll
+        for (int s = 0; s < 8; s++) rows_of_slot[s] = s;
+        gu_task<BF16>(stage, xfrag, xS, xC, T, m->cols, task * 16, red, warp, lane, A.act_sh,
+                      rows_of_slot, T);
+      } else {
+        router_task<BF16>(A, L, stage, xh, task - 32, warp, lane);
+      }
+      __syncthreads();
+      if (m->fail) return;
+      release(L, i, nR_my, dR);
+    }
+    if (!grid_sync(A.bar, epoch, A.status, m)) return;
+
+    // ---------------- phase E: top-k + grouping
+    if (A.r.idx_in) {
+      if (tid < npos) {
+        m->idx[tid] = A.r.idx_in[tid];
+        m->w[tid] = A.r.w_in[tid];
+      }
+    } else if (warp < T) {
+      topk_warp(A.logits, A.r.bias, warp, lane, m->idx, m->w);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && tid < npos) {
+      if (A.idx_out) A.idx_out[(size_t)l * npos + tid] = m->idx[tid];
+      if (A.w_out) A.w_out[(size_t)l * npos + tid] = m->w[tid];
+    }
+    if (tid < npos) {
+      int rec = A.r.rec_of_pos ? A.r.rec_of_pos[tid] : m->idx[tid];
+      if (rec < 0 || (unsigned)rec >= L.bank_records) {
+        set_status(A.status, kStatusDevice);
+        rec = 0;
+      }
+      m->rec_pos[tid] = rec;
+    }
+    __syncthreads();
+    if (tid < npos) {
+      const int my_key = (m->rec_pos[tid] << 6) | tid;
+      int my_rank = 0;
+      for (int j = 0; j < npos; j++) my_rank += ((m->rec_pos[j] << 6) | j) < my_key;
+      m->skey[my_rank] = my_key;
+    }
+    __syncthreads();
+    if (tid < npos) {
+      const int rec = m->skey[tid] >> 6;
+      m->sorted_pos[tid] = m->skey[tid] & 63;
+      const bool start = (tid == 0) || (rec != (m->skey[tid - 1] >> 6));
+      int gidx = 0;  // number of group starts before tid
+      for (int j = 1; j <= tid; j++) gidx += (m->skey[j] >> 6) != (m->skey[j - 1] >> 6);
+      if (start) {
+        m->grp_start[gidx] = tid;
+        m->grp_rec[gidx] = rec;
+      }
+      if (tid == npos - 1) m->ng = gidx + 1;
+    }
+    __syncthreads();
+    const int ng = m->ng;
+    if (tid < ng) m->grp_cnt[tid] = (tid + 1 < ng ? m->grp_start[tid + 1] : npos) - m->grp_start[tid];
+    // L2 prefetch of the routed experts' down projections (9 x 64 KB each)
+    if (tid == 0)
+      for (int c = blockIdx.x; c < ng * 9; c += G)
+        prefetch_l2(L.bank + (uint64_t)m->grp_rec[c / 9] * L.stride + kOffDownW + (size_t)(c % 9) * 65536, 65536);
+    __syncthreads();
+
+    // ---------------- phase E tasks: routed gate/up (ng x 32), shared down (32)
+    {
+      const PhaseE dE{ng * 32};
+      const int nE_my = n_mine(ng * 32 + 32);
+      prime(L, nE_my, dE);
+      bool sh_staged = false;
+      for (int i = 0; i < nE_my; i++) {
+        const int task = dE.task(i);
+        if (task >= dE.n_gu && !sh_staged) {
+          stage_block<false>(A.act_sh, T, 8, kInter, T, shfrag, shS, shC);
+          __syncthreads();
+          sh_staged = true;
+        }
+        unsigned char* stage = acquire(i);
+        if (task < dE.n_gu) {
+          const int gi = task >> 5, tile = task & 31;
+          const int cnt = m->grp_cnt[gi], stt = m->grp_start[gi];
+          int cols[8], pos_of_slot[8];
+#pragma unroll
+          for (int s2 = 0; s2 < 8; s2++) {
+            cols[s2] = s2 < cnt ? (m->sorted_pos[stt + s2] >> 3) : -1;
+            pos_of_slot[s2] = s2 < cnt ? m->sorted_pos[stt + s2] : 0;
+          }
+          gu_task<BF16>(stage, xfrag, xS, xC, T, cols, tile * 16, red, warp, lane, A.act,
+                        pos_of_slot, cnt);
+        } else {
+          // 64 rows = 4 row tiles (warp & 3) x 4 K-quarters (warp >> 2)
+          const int row0 = (task - dE.n_gu) * kShDnRows;
+          const int rt = warp & 3, kq = warp >> 2;
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint8_t* rows = stage + rt * 16 * kDnPitch;
+          const uint16_t* s = reinterpret_cast<const uint16_t*>(stage + kShDnRows * kDnPitch) + rt * 16 * 8;
+          const uint16_t* b = reinterpret_cast<const uint16_t*>(stage + kShDnRows * kDnPitch + kShDnRows * 16) + rt * 16 * 8;
+          mma_tile_smem<BF16, 2>(rows, kDnPitch, kq * 2, s, b, 8, shfrag, shS, shC, T,
+                                 m->cols, acc, lane);
+          const int g = lane >> 2, t = lane & 3;
+          float* r = red + (kq * 4 + rt) * 128;
+          r[g * 8 + 2 * t] = acc[0];
+          r[g * 8 + 2 * t + 1] = acc[1];
+          r[(g + 8) * 8 + 2 * t] = acc[2];
+          r[(g + 8) * 8 + 2 * t + 1] = acc[3];
+          __syncthreads();
+          const int rr = tid >> 3, slot = tid & 7;  // 64 rows x 8 slots
+          if (slot < T) {
+            const int rt2 = rr >> 4, row = rr & 15;
+            float v = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; q++) v = __fadd_rn(v, red[(q * 4 + rt2) * 128 + row * 8 + slot]);
+            A.y_sh[slot * kHidden + row0 + rr] = v;
+          }
+        }
+        __syncthreads();
+        if (m->fail) return;
+        release(L, i, nE_my, dE);
+      }
+    }
+    if (!grid_sync(A.bar, epoch, A.status, m)) return;
+
+    // ---------------- phase D: routed down + combine + norm partials
+    if (li + 1 < A.n_layers && tid == 0) {
+      const LayerW& N = A.layers[li + 1];
+      // router 8 x 64 KB, router scales/biases, shared record 27 x 64 KB
+      for (int c = blockIdx.x; c < 8 + 2 + 27; c += G) {
+        if (c < 8) prefetch_l2(N.rw + (size_t)c * 65536, 65536);
+        else if (c == 8) prefetch_l2(N.rs, 16384);
+        else if (c == 9) prefetch_l2(N.rb, 16384);
+        else prefetch_l2(N.shared + (size_t)(c - 10) * 65536, 65536);
+      }
+    }
+    {
+      const int nchunk = (ng + kDnGroupsPerStage - 1) / kDnGroupsPerStage;
+      const PhaseD dD{nchunk};
+      const int nD_my = n_mine(kOutTiles) * nchunk;
+      prime(L, nD_my, dD);
+      if (nD_my > 0) {
+        // stage the routed activations once
+        stage_block<false>(A.act, npos, 8, kInter, npos, afrag, aS, aC);
+        __syncthreads();
+      }
+      for (int i = 0; i < nD_my; i++) {
+        unsigned char* stage = acquire(i);
+        const int tile = dD.tile(i), chunk = i % nchunk;
+        const int row0 = tile * 16;
+        const int gbeg = chunk * kDnGroupsPerStage;
+        const int gend = gbeg + kDnGroupsPerStage < ng ? gbeg + kDnGroupsPerStage : ng;
+        for (int gi = gbeg + warp; gi < gend; gi += kFWarps) {
+          const unsigned char* gs = stage + (gi - gbeg) * kDnGroupBytes;
+          const int cnt = m->grp_cnt[gi], stt = m->grp_start[gi];
+          int cols[8];
+#pragma unroll
+          for (int s2 = 0; s2 < 8; s2++) cols[s2] = s2 < cnt ? m->sorted_pos[stt + s2] : -1;
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_tile_smem<BF16, 8>(gs, kDnPitch, 0, reinterpret_cast<const uint16_t*>(gs + 16 * kDnPitch),
+                                 reinterpret_cast<const uint16_t*>(gs + 16 * kDnPitch + 256), 8, afrag,
+                                 aS, aC, npos, cols, acc, lane);
+          const int g = lane >> 2, t = lane & 3;
+          const int p0 = 2 * t < cnt ? m->sorted_pos[stt + 2 * t] : -1;
+          const int p1 = 2 * t + 1 < cnt ? m->sorted_pos[stt + 2 * t + 1] : -1;
+          if (p0 >= 0) {
+            red[p0 * 16 + g] = acc[0];
+            red[p0 * 16 + g + 8] = acc[2];
+          }
+          if (p1 >= 0) {
+            red[p1 * 16 + g] = acc[1];
+            red[p1 * 16 + g + 8] = acc[3];
+          }
+        }
+        if (chunk == nchunk - 1) {
+          __syncthreads();
+          if (tid < 16 * T) {
+            const int t = tid >> 4, row = tid & 15;
+            const int r = row0 + row;
+            const float c = __ldcg(A.coef + t);
+            const float coeff = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-c)));
+            const float sh = __fmul_rn(__ldcg(A.y_sh + t * kHidden + r), coeff);
+            float routed = __fmul_rn(red[(t * kTopK) * 16 + row], m->w[t * kTopK]);
+#pragma unroll
+            for (int k = 1; k < kTopK; k++)
+              routed = __fadd_rn(routed, __fmul_rn(red[(t * kTopK + k) * 16 + row], m->w[t * kTopK + k]));
+            const float base = res ? __ldcg(res + t * kHidden + r) : 0.f;
+            const float v = __fadd_rn(__fadd_rn(base, sh), routed);
+            o[t * kHidden + r] = v;
+            red[1024 + t * 16 + row] = v;
+          }
+          __syncthreads();
+          if (tid < T) {
+            float acc = 0.f;
+            for (int row = 0; row < 16; row++) {
+              const float v = red[1024 + tid * 16 + row];
+              acc = __fmaf_rn(v, v, acc);
+            }
+            A.ssq[tile * kFMaxT + tid] = acc;
+          }
+        }
+        __syncthreads();
+        if (m->fail) return;
+        release(L, i, nD_my, dD);
+      }
+    }
+    if (li + 1 < A.n_layers)
+      if (!grid_sync(A.bar, epoch, A.status, m)) return;
+  }
+}
+
+int g_fused_grid[64] = {};
+
+}  // namespace
+
+size_t fused_workspace_bytes(int T) {
+  (void)T;
+  size_t b = 0;
+  auto a = [](size_t n) { return (n + 255) & ~(size_t)255; };
+  b += a(4 * kFMaxT * kExperts);     // logits
+  b += a(4 * kFMaxT);                // coef
+  b += a(4 * kFMaxPos * kInter);     // act
+  b += a(4 * kFMaxT * kInter);       // act_sh
+  b += a(4 * kFMaxT * kHidden);      // y_sh
+  b += 2 * a(4 * kFMaxT * kHidden);  // h ping-pong
+  b += a(4 * kOutTiles * kFMaxT);    // ssq
+  b += a(256);                       // barrier counter
+  return b;
+}
+
+cudaError_t fused_init_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(k_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmMax);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_fused<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmMax);
+}
+
+cudaError_t fused_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16, int T,
+                        const uint16_t* x, const float* residual, float* out, float eps,
+                        const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
+                        int* status, Prof* prof) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const SmLayout SL = sm_layout(T);
+  if (SL.nstages < 2) return cudaErrorInvalidValue;
+  const int smem = SL.total;
+  if (g_fused_grid[dev] == 0) {
+    int sms = 0, per = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per, bf16 ? (const void*)k_fused<true> : (const void*)k_fused<false>, kFThreads, kSmMax);
+    if (e != cudaSuccess) return e;
+    if (per < 1) return cudaErrorCooperativeLaunchTooLarge;
+    g_fused_grid[dev] = sms;
+  }
+  char* p = static_cast<char*>(workspace);
+  auto take = [&](size_t n) {
+    char* q = p;
+    p += (n + 255) & ~(size_t)255;
+    return q;
+  };
+  FusedArgs A;  // layers by value: copied into the launch's parameter space
+  A.T = T;
+  A.total_layers = n_layers;
+  A.x0 = x;
+  A.res0 = residual;
+  A.out = out;
+  A.eps = eps;
+  A.r = r;
+  A.idx_out = idx_out;
+  A.w_out = w_out;
+  A.logits = reinterpret_cast<float*>(take(4 * kFMaxT * kExperts));
+  A.coef = reinterpret_cast<float*>(take(4 * kFMaxT));
+  A.act = reinterpret_cast<float*>(take(4 * kFMaxPos * kInter));
+  A.act_sh = reinterpret_cast<float*>(take(4 * kFMaxT * kInter));
+  A.y_sh = reinterpret_cast<float*>(take(4 * kFMaxT * kHidden));
+  A.h0 = reinterpret_cast<float*>(take(4 * kFMaxT * kHidden));
+  A.h1 = reinterpret_cast<float*>(take(4 * kFMaxT * kHidden));
+  A.ssq = reinterpret_cast<float*>(take(4 * kOutTiles * kFMaxT));
+  A.bar = reinterpret_cast<unsigned*>(take(256));
+  A.status = status;
+  for (int l0 = 0; l0 < n_layers; l0 += kFMaxLayers) {
+    const int n = n_layers - l0 < kFMaxLayers ? n_layers - l0 : kFMaxLayers;
+    A.first_layer = l0;
+    A.n_layers = n;
+    for (int i = 0; i < n; i++) A.layers[i] = layers[l0 + i];
+    e = cudaMemsetAsync(A.bar, 0, 256, st);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g_fused_grid[dev]);
+    cfg.blockDim = dim3(kFThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // optional timing events around the launch (bench harness)
+    int slot = -1;
+    unsigned flags = cudaEventRecordDefault;
+    if (prof && prof->kernel == kKFused && prof->n < prof->cap) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cs);
+      if (cs == cudaStreamCaptureStatusActive) flags = cudaEventRecordExternal;
+      slot = prof->n++;
+      cudaEventRecordWithFlags(prof->ev0[slot], st, flags);
+    }
+    if (bf16)
+      e = cudaLaunchKernelEx(&cfg, k_fused<true>, A);
+    else
+      e = cudaLaunchKernelEx(&cfg, k_fused<false>, A);
+    if (slot >= 0) cudaEventRecordWithFlags(prof->ev1[slot], st, flags);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace qf

@@ -47,7 +47,7 @@ struct Prof {
   cudaEvent_t* ev0 = nullptr;
   cudaEvent_t* ev1 = nullptr;
 };
-enum KernelId { kKRouter = 0, kKTopk = 1, kKGateUp = 2, kKDown = 3, kKCombine = 4 };
+enum KernelId { kKRouter = 0, kKTopk = 1, kKGateUp = 2, kKDown = 3, kKCombine = 4, kKFused = 5 };
 
 struct RoutingArgs {
   const float* bias;
@@ -67,6 +67,16 @@ cudaError_t router_logits(cudaStream_t st, const LayerW& L, bool bf16, int T, co
                           float* logits, float* coef, int* status);
 cudaError_t router_topk(cudaStream_t st, int T, const float* logits, const float* bias,
                         int* idx, float* w, int* status);
+
+// ---- persistent fused decode for T <= 8 (qf_fused.cu)
+constexpr int kFusedMaxTokens = 8;
+size_t fused_workspace_bytes(int T);
+cudaError_t fused_init_attributes();
+// layers: host array of n_layers descriptors (passed by value to the kernel)
+cudaError_t fused_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16, int T,
+                        const uint16_t* x, const float* residual, float* out, float eps,
+                        const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
+                        int* status, Prof* prof);
 
 // ---- dispatch plan (qf_route.cu)
 size_t dispatch_workspace_bytes(int T);

@@ -66,6 +66,10 @@ extern "C" qf_status qf_moe_block_forward_static(int32_t scale_dtype, const qf_m
   if (T < 1 || T > qf::kStaticMaxTokens) return QF_ERR_ARG;
   if (scale_dtype != QF_SCALE_F16 && scale_dtype != QF_SCALE_BF16) return QF_ERR_ARG;
   if (!layer || !x || !out || (reinterpret_cast<uintptr_t>(x) % 16) != 0) return QF_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(layer->router_w) | reinterpret_cast<uintptr_t>(layer->router_s) |
+       reinterpret_cast<uintptr_t>(layer->router_b) | reinterpret_cast<uintptr_t>(layer->shared_record) |
+       reinterpret_cast<uintptr_t>(layer->expert_bank)) % 16 != 0)
+    return QF_ERR_ARG;
   if (!layer->router_w || !layer->router_s || !layer->router_b || !layer->coef_w ||
       !layer->coef_s || !layer->coef_b || !layer->shared_record || !layer->expert_bank ||
       layer->record_stride < qf::kRecordBytes || (layer->record_stride % 16) != 0 ||

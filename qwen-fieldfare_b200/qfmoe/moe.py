@@ -243,7 +243,7 @@ def stack_forward(ctx: MoEContext, plan: StackPlan, x: torch.Tensor,
     return (out, idx, w) if return_routing else out
 
 
-KERNEL_IDS = {"router": 0, "topk": 1, "gate_up": 2, "down": 3, "combine": 4}
+KERNEL_IDS = {"router": 0, "topk": 1, "gate_up": 2, "down": 3, "combine": 4, "fused": 5}
 
 
 def profile_begin(ctx: MoEContext, kernel: str, max_launches: int = 4096) -> None:

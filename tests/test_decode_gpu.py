@@ -188,11 +188,12 @@ def test_block_bf16_scales():
     assert max_rel(out.cpu().numpy(), ref["out"]) < TOL
 
 
-def test_stack_equals_chained_blocks_with_oracle_norm(ctx, layers, oracle_layers):
+@pytest.mark.parametrize("T", [3, 12])
+def test_stack_equals_chained_blocks_with_oracle_norm(ctx, layers, oracle_layers, T):
     """Two stacked blocks == block 0, the oracle's RMSNorm of its output, block 1:
-    bitwise, which pins the in-kernel RMSNorm (deltanet.metal:18-53) to the oracle."""
+    bitwise, which pins the in-kernel RMSNorm (deltanet.metal:18-53) to the oracle.
+    T = 3 runs the persistent kernel, T = 12 the per-kernel path."""
     from qfmoe import StackPlan, block_forward, stack_forward
-    T = 3
     x = hidden(T, tok0=40)
     plan = StackPlan([layers[(0, False)], layers[(1, False)]])
     out, idx, _ = stack_forward(ctx, plan, x.cuda(), eps=1e-6, return_routing=True)
@@ -238,3 +239,36 @@ def test_dispatch_plan_matches_oracle(ctx):
         assert np.array_equal(c.cpu().numpy(), rc)
         assert np.array_equal(o.cpu().numpy(), ro)
         assert np.array_equal(perm.cpu().numpy(), rp)
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_persistent_and_per_kernel_paths_agree(ctx, layers, oracle_layers, T):
+    """T <= 8 runs the persistent kernel; with per-kernel timing enabled the same
+    call runs the five-kernel path.  Both must meet the oracle bar."""
+    from qfmoe import block_forward, profile_begin, profile_end
+    x = hidden(T, tok0=700)
+    o1, i1, _ = block_forward(ctx, layers[(1, False)], x.cuda(), return_routing=True)
+    profile_begin(ctx, "gate_up", 16)
+    o2, i2, _ = block_forward(ctx, layers[(1, False)], x.cuda(), return_routing=True)
+    ms, n = profile_end(ctx)
+    assert n == 1 and ms > 0
+    ref = O.block(oracle_layers[1], x.numpy().view(np.uint16), threads=8)
+    assert np.array_equal(i1.cpu().numpy(), ref["idx"])
+    assert np.array_equal(i2.cpu().numpy(), ref["idx"])
+    assert max_rel(o1.cpu().numpy(), ref["out"]) < TOL
+    assert max_rel(o2.cpu().numpy(), ref["out"]) < TOL
+
+
+def test_stack_long_chain_matches_blocks(ctx, layers):
+    """A 5-layer stack (layers 0,1,0,1,0) equals the chain of single blocks with the
+    in-kernel norm emulated by the oracle, bitwise."""
+    from qfmoe import StackPlan, block_forward, stack_forward
+    T = 2
+    x = hidden(T, tok0=77)
+    seq = [layers[(0, False)], layers[(1, False)]] * 2 + [layers[(0, False)]]
+    out = stack_forward(ctx, StackPlan(seq), x.cuda(), eps=1e-6)
+    h = block_forward(ctx, seq[0], x.cuda())
+    for L in seq[1:]:
+        xn = torch.from_numpy(O.rmsnorm_to_f16(h.cpu().numpy(), 1e-6).view(np.float16)).cuda()
+        h = block_forward(ctx, L, xn, h)
+    assert torch.equal(out, h)

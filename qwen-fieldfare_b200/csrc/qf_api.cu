@@ -129,7 +129,7 @@ qf_status qf_moe_create(const qf_moe_dims* dims, int device, qf_moe** out) {
     return QF_ERR_OOM;
   }
   if (cudaMemset(h->d_status, 0, 256) != cudaSuccess || qf::decode_init_attributes() != cudaSuccess ||
-      qf::fused_init_attributes() != cudaSuccess) {
+      qf::fused_init_attributes() != cudaSuccess || qf::prefill_init_attributes() != cudaSuccess) {
     cudaFree(h->d_status);
     delete h;
     return QF_ERR_CUDA;
@@ -221,8 +221,11 @@ qf_status qf_moe_dispatch_plan(qf_moe* h, const int32_t* idx, int32_t T, int32_t
 
 qf_status qf_moe_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
   if (!h || !bytes) return QF_ERR_ARG;
-  if (T < 1 || T > qf::kDecodeMaxTokens)
-    return fail(h, QF_ERR_ARG, "T must be in [1, 64] for the decode path");
+  if (T < 1 || T > qf::kPrefillMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
+  if (T > qf::kDecodeMaxTokens) {
+    *bytes = qf::prefill_workspace_bytes(T);
+    return QF_OK;
+  }
   const size_t a = qf::decode_workspace_bytes(T);
   const size_t b = T <= qf::kFusedMaxTokens ? qf::fused_workspace_bytes(T) : 0;
   *bytes = a > b ? a : b;
@@ -237,8 +240,7 @@ qf_status qf_moe_block_forward(qf_moe* h, const qf_moe_layer* layer, int32_t T, 
   qf::LayerW w;
   qf_status s = layer_to_w(h, layer, &w);
   if (s != QF_OK) return s;
-  if (T < 1 || T > qf::kDecodeMaxTokens)
-    return fail(h, QF_ERR_ARG, "T must be in [1, 64] (decode path)");
+  if (T < 1 || T > qf::kPrefillMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
   if (!x || !out || !aligned(x, 16)) return fail(h, QF_ERR_ARG, "x (16-B aligned) and out are required");
   size_t need = 0;
   qf_moe_workspace_size(h, T, &need);
@@ -250,7 +252,12 @@ qf_status qf_moe_block_forward(qf_moe* h, const qf_moe_layer* layer, int32_t T, 
   DeviceGuard g(h->device);
   const bool bf16 = h->dims.scale_dtype == QF_SCALE_BF16;
   cudaError_t e;
-  if (T <= qf::kFusedMaxTokens && (h->prof.kernel < 0 || h->prof.kernel == qf::kKFused)) {
+  if (T > qf::kDecodeMaxTokens) {
+    if (w.bank_records < (uint32_t)qf::kExperts || r.rec_of_pos)
+      return fail(h, QF_ERR_ARG, "the prefill path needs a resident bank of 256 experts");
+    e = qf::prefill_block(stream_of(h), w, bf16, T, x, residual, out, r, idx_out, w_out, workspace,
+                          h->d_status, &h->prof);
+  } else if (T <= qf::kFusedMaxTokens && (h->prof.kernel < 0 || h->prof.kernel == qf::kKFused)) {
     if (workspace_bytes < qf::fused_workspace_bytes(T))
       return fail(h, QF_ERR_ARG, "workspace too small");
     e = qf::fused_stack(stream_of(h), &w, 1, bf16, T, x, residual, out, 1e-6f, r, idx_out, w_out,

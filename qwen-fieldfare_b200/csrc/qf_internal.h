@@ -78,6 +78,16 @@ cudaError_t fused_stack(cudaStream_t st, const LayerW* layers, int n_layers, boo
                         const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
                         int* status, Prof* prof);
 
+// ---- prefill path, T > 64 (qf_prefill.cu)
+constexpr int kPrefillMaxTokens = 32768;
+size_t prefill_workspace_bytes(int T);
+cudaError_t prefill_init_attributes();
+cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
+                                  const uint16_t* x, float* logits, float* coef);
+cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                          const float* residual, float* out, const RoutingArgs& r, int* idx_out,
+                          float* w_out, void* workspace, int* status, Prof* prof);
+
 // ---- dispatch plan (qf_route.cu)
 size_t dispatch_workspace_bytes(int T);
 cudaError_t dispatch_plan_ws(cudaStream_t st, const int* idx, int T, int* counts, int* offsets,

@@ -81,9 +81,9 @@ typedef struct qf_moe_layer {
     const uint8_t *coef_w;     /* [hidden] Q8 codes of the shared-expert gate */
     const uint16_t *coef_s;    /* [hidden/64] */
     const uint16_t *coef_b;
-    const uint8_t *shared_record; /* one expert record: the shared expert */
-    const uint8_t *expert_bank;   /* record 0 of the routed bank / slot arena */
-    uint64_t record_stride;       /* bytes between records (>= 1,769,472, multiple of 16) */
+    const uint8_t *shared_record; /* one expert record: the shared expert (32-byte aligned) */
+    const uint8_t *expert_bank;   /* record 0 of the routed bank / slot arena (32-byte aligned) */
+    uint64_t record_stride;       /* bytes between records (>= 1,769,472, multiple of 32) */
     uint32_t bank_records;        /* records in the bank (experts, or cache slots); a
                                      routed record index >= this is a device error */
     uint32_t reserved;            /* must be 0 */
@@ -153,8 +153,9 @@ qf_status qf_moe_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
  *   out: fp32 [T * hidden]; idx_out/w_out: optional [T * top_k];
  *   routing: optional; workspace: >= qf_moe_workspace_size bytes (256-B aligned).
  * T in [1, 8] runs one persistent cooperative kernel (all phases of the block,
- * grid barriers between them); T in [9, 64] runs five kernels per block.
- * Larger T is rejected (QF_ERR_ARG) until the prefill path is built. */
+ * grid barriers between them); T in [9, 64] runs five kernels per block;
+ * T in [65, 32768] (prefill) runs the grouped tensor-core path, which needs a
+ * bank of all 256 experts (bank_records >= 256) and no record_of_pos. */
 qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
                                const uint16_t *x, const float *residual, float *out,
                                const qf_routing *routing, int32_t *idx_out, float *w_out,

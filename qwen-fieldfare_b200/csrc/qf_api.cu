@@ -64,13 +64,14 @@ qf_status layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
   if (!l->router_w || !l->router_s || !l->router_b || !l->coef_w || !l->coef_s || !l->coef_b ||
       !l->shared_record || !l->expert_bank)
     return fail(h, QF_ERR_ARG, "layer descriptor has a NULL weight pointer");
-  if (l->record_stride < qf::kRecordBytes || (l->record_stride % 16) != 0)
-    return fail(h, QF_ERR_ARG, "record_stride must be >= 1769472 and a multiple of 16");
-  if (!aligned(l->router_w, 16) || !aligned(l->coef_w, 16) || !aligned(l->shared_record, 16) ||
-      !aligned(l->expert_bank, 16) || !aligned(l->router_s, 16) || !aligned(l->router_b, 16) ||
-      !aligned(l->coef_s, 2) || !aligned(l->coef_b, 2))
-    return fail(h, QF_ERR_ARG,
-                "router codes/scales/biases, shared record and bank must be 16-byte aligned");
+  if (l->record_stride < qf::kRecordBytes || (l->record_stride % 32) != 0)
+    return fail(h, QF_ERR_ARG, "record_stride must be >= 1769472 and a multiple of 32");
+  if (!aligned(l->router_w, 16) || !aligned(l->coef_w, 16) || !aligned(l->router_s, 16) ||
+      !aligned(l->router_b, 16) || !aligned(l->coef_s, 2) || !aligned(l->coef_b, 2))
+    return fail(h, QF_ERR_ARG, "router codes/scales/biases must be 16-byte aligned");
+  // expert codes are read 32 bytes at a time
+  if (!aligned(l->shared_record, 32) || !aligned(l->expert_bank, 32))
+    return fail(h, QF_ERR_ARG, "shared record and bank must be 32-byte aligned");
   if (l->bank_records == 0 || l->bank_records >= (1u << 23))
     return fail(h, QF_ERR_ARG, "bank_records must be in [1, 2^23)");
   if (l->reserved != 0) return fail(h, QF_ERR_ARG, "reserved field must be 0");

@@ -713,26 +713,6 @@ cudaError_t router_topk(cudaStream_t st, int T, const float* logits, const float
 }
 
 namespace {
-struct ProfScope {
-  Prof* p;
-  cudaStream_t st;
-  int slot = -1;
-  unsigned flags = cudaEventRecordDefault;
-  ProfScope(Prof* prof, int kernel, cudaStream_t s) : p(prof), st(s) {
-    if (p && p->kernel == kernel && p->n < p->cap) {
-      // inside stream capture a plain record only orders streams; an external
-      // record becomes a timing node of the graph
-      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-      cudaStreamIsCapturing(st, &cs);
-      if (cs == cudaStreamCaptureStatusActive) flags = cudaEventRecordExternal;
-      slot = p->n++;
-      cudaEventRecordWithFlags(p->ev0[slot], st, flags);
-    }
-  }
-  ~ProfScope() {
-    if (slot >= 0) cudaEventRecordWithFlags(p->ev1[slot], st, flags);
-  }
-};
 }  // namespace
 
 cudaError_t decode_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,

@@ -49,6 +49,28 @@ struct Prof {
 };
 enum KernelId { kKRouter = 0, kKTopk = 1, kKGateUp = 2, kKDown = 3, kKCombine = 4, kKFused = 5 };
 
+// Records the event pair of one launch of `kernel` when it is being profiled.
+struct ProfScope {
+  Prof* p;
+  cudaStream_t st;
+  int slot = -1;
+  unsigned flags = cudaEventRecordDefault;
+  ProfScope(Prof* prof, int kernel, cudaStream_t s) : p(prof), st(s) {
+    if (p && p->kernel == kernel && p->n < p->cap) {
+      // inside stream capture a plain record only orders streams; an external
+      // record becomes a timing node of the graph
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cs);
+      if (cs == cudaStreamCaptureStatusActive) flags = cudaEventRecordExternal;
+      slot = p->n++;
+      cudaEventRecordWithFlags(p->ev0[slot], st, flags);
+    }
+  }
+  ~ProfScope() {
+    if (slot >= 0) cudaEventRecordWithFlags(p->ev1[slot], st, flags);
+  }
+};
+
 struct RoutingArgs {
   const float* bias;
   const int* idx_in;

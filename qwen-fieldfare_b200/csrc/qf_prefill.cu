@@ -5,20 +5,36 @@
 //   k_router_prefill  router logits in the reference lane order (bit-exact)
 //   k_topk            top-8 / softmax / renormalise (with the harness bias)
 //   dispatch plan     counts, offsets, stable permutation by (expert, token, k)
-//   k_tile_map        one entry per 128-row tile of every expert (+ shared)
-//   k_moe_gemm<0>     gate/up: X[perm rows] . [G;U]^T -> SiLU(g)*u (fp16 act)
-//   k_moe_gemm<1>     down: act . D^T * routing weight -> per-position rows
-//   k_combine         residual + sigmoid(c) * shared + sum_k in router order
+//   k_gather_rows     token rows in expert order (+ all T tokens for the
+//                     shared expert after them), K-permuted, fp16
+//   k_tile_list       128-row tiles of every expert (+ shared), longest first
+//   k_grouped<0>      gate/up: SiLU(G x) * (U x) -> fp16 act rows
+//   k_grouped<1>      down: D act -> fp32 y rows
+//   k_combine         residual + sigmoid(c) * y_shared + sum_k w_k y_k (router order)
 //
-// k_moe_gemm: one CTA per (128-row tile, N tile).  A (token rows, fp16) is
-// gathered with 16-byte cp.async into the 128-byte-swizzled K-major layout;
-// the expert's Q4 codes are copied the same way and dequantised to fp16
-// (w = q*s + b, one rounding) into the B operand; one thread issues
-// tcgen05.mma (M=128, N=256, K=16 x 4 per 64-column group) accumulating in
-// TMEM; completions are tracked with tcgen05.commit on mbarriers so loads,
-// dequant and MMA of consecutive K steps overlap.  The epilogue reads TMEM
-// with tcgen05.ld.
+// Row space shared by the gathered x, act and y buffers: rows [0, P) are the
+// P = 8T routed positions sorted by (expert, token, k); rows [P, P + T) are
+// the shared expert's tokens.  Expert e owns rows [offsets[e], offsets[e+1])
+// with offsets[256] = P, so the shared expert is simply expert 256.
+//
+// k_grouped computes D[weight row][token] = W[row][:] . X[token][:] with the
+// expert's weights as the MMA's A operand in TENSOR MEMORY and the token rows
+// as the B operand in shared memory.  Dequantised weights never touch shared
+// memory: producer threads turn Q4 codes (read straight into registers) into
+// fp16 and write them to TMEM with tcgen05.st, so shared-memory bandwidth is
+// spent only on the token rows, which arrive by TMA (one 2-D tile load per
+// 64-column step).
+//
+// K order inside every 8-element group is permuted to (0,4,1,5,2,6,3,7) in
+// BOTH operands (the dot product is unchanged): that is the order in which
+// the nibble extraction produces fp16 pairs, so the dequant needs no byte
+// permutes.  k_gather_rows permutes x; act rows are written permuted by the
+// gate/up epilogue.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <math.h>
+
+#include <algorithm>
 
 #include "qf_internal.h"
 
@@ -32,7 +48,6 @@ constexpr int kStatusTimeout = -6;
 __device__ __forceinline__ uint32_t s_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 // K-major, 128-byte swizzle, 8-row groups 1024 bytes apart
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   uint64_t d = 0;
@@ -43,16 +58,13 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;
   return d;
 }
-__device__ __forceinline__ void cp16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s_u32(bar)), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(bar)) : "memory");
 }
-__device__ __forceinline__ bool mbar_wait_p(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = s_u32(bar);
   for (unsigned i = 0; i < kSpin; i++) {
     uint32_t done;
@@ -64,6 +76,77 @@ __device__ __forceinline__ bool mbar_wait_p(uint64_t* bar, uint32_t parity) {
     if (done) return true;
   }
   return false;
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(bytes) : "memory");
+}
+// 2-D tiled TMA load (128-byte swizzle in the tensor map) completing on bar
+__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          s_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s_u32(bar))
+               : "memory");
+}
+// D[tmem d] (+)= A[tmem a] . B[smem desc]^T
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(
+          d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%"
+      "20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 32 bytes of Q4 codes straight into registers (read once; no L1 allocation)
+__device__ __forceinline__ void ld_codes32(const uint8_t* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// (x0..x7) -> (x0,x4,x1,x5,x2,x6,x3,x7): the K order of the GEMM operands
+__device__ __forceinline__ uint4 permute8(uint4 v) {
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                    __byte_perm(v.y, v.w, 0x7632));
 }
 
 // ------------------------------------------------------------------ router
@@ -164,343 +247,415 @@ __global__ void __launch_bounds__(kRtThreads) k_router_prefill(LayerW L, int T,
   }
 }
 
-// ------------------------------------------------------------------ tile map
-// tiles[i] = (expert, first row); expert 256 = the shared expert (all T tokens).
-__global__ void k_tile_map(const int* __restrict__ counts, int T, int2* __restrict__ tiles,
-                           int* __restrict__ n_tiles) {
-  if (threadIdx.x != 0) return;
-  int n = 0;
-  for (int e = 0; e <= kExperts; e++) {
-    const int cnt = e < kExperts ? counts[e] : T;
-    for (int m0 = 0; m0 < cnt; m0 += 128) tiles[n++] = make_int2(e, m0);
+// ------------------------------------------------------------------ row gather
+// xs[r] = permute8(x[perm[r] / 8]) for r < P, xs[P + t] = permute8(x[t]);
+// one warp per row, 16-byte vectors.
+__global__ void __launch_bounds__(256) k_gather_rows(const int* __restrict__ perm, int P, int T,
+                                                     const uint4* __restrict__ x, uint4* __restrict__ xs) {
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= P + T) return;
+  const int src = r < P ? (perm[r] >> 3) : r - P;
+  const uint4* s = x + (size_t)src * (kHidden / 8);
+  uint4* d = xs + (size_t)r * (kHidden / 8);
+  uint4 v[kHidden / 8 / 32];
+#pragma unroll
+  for (int j = 0; j < kHidden / 8 / 32; j++) v[j] = __ldg(s + lane + 32 * j);
+#pragma unroll
+  for (int j = 0; j < kHidden / 8 / 32; j++) d[lane + 32 * j] = permute8(v[j]);
+}
+
+// ------------------------------------------------------------------ tile list
+// tiles[i] = (expert, first row, rows, first row of the expert in the row
+// space); expert 256 = the shared expert over all T tokens (rows P..P+T-1).  Full kTileRows-row tiles
+// come first, then partial tiles by decreasing size (ties: lower expert
+// first), so a round-robin over persistent CTAs hands the longest units out
+// first.
+constexpr int kTileRows = 128;
+constexpr int kListThreads = 288;  // one thread per expert and the shared expert
+
+__global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restrict__ counts,
+                                                             const int* __restrict__ offsets, int T,
+                                                             int4* __restrict__ tiles, int* __restrict__ n_tiles) {
+  __shared__ int s_rem[kListThreads];
+  __shared__ int s_warp[kListThreads / 32];
+  const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+  int cnt = 0, base = 0;
+  if (e < kExperts) {
+    cnt = counts[e];
+    base = offsets[e];
+  } else if (e == kExperts) {
+    cnt = T;
+    base = T * kTopK;
   }
-  *n_tiles = n;
+  const int full = cnt / kTileRows, rem = cnt % kTileRows;
+  s_rem[e] = rem;
+  int v = full;  // inclusive warp scan of the full-tile counts
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
+  }
+  if (lane == 31) s_warp[warp] = v;
+  __syncthreads();
+  int before = 0, total_full = 0;
+  for (int w = 0; w < kListThreads / 32; w++) {
+    const int s = s_warp[w];
+    if (w < warp) before += s;
+    total_full += s;
+  }
+  const int first = before + v - full;
+  for (int j = 0; j < full; j++) tiles[first + j] = make_int4(e, j * kTileRows, kTileRows, base);
+  if (rem > 0) {
+    int pos = 0;
+    for (int o = 0; o < kListThreads; o++) {
+      const int r2 = s_rem[o];
+      pos += (r2 > rem || (r2 == rem && o < e)) ? 1 : 0;
+    }
+    tiles[total_full + pos] = make_int4(e, full * kTileRows, rem, base);
+  }
+  const int n_part = __syncthreads_count(rem > 0);
+  if (e == 0) *n_tiles = total_full + n_part;
 }
 
 // ------------------------------------------------------------------ grouped GEMM
-constexpr int kGThreads = 256;
-constexpr int kStages = 4;  // A / code stages in flight
-constexpr int kABytes = 128 * 128;   // 128 rows x 64 fp16
-constexpr int kBBytes = 256 * 128;   // 256 rows x 64 fp16
-constexpr int kCodeBytes = 256 * 32; // 256 rows x 64 nibbles
-// shared memory: A[kStages] | B fp16 [2] | codes[kStages] | scales | biases | barriers
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kABytes;
-constexpr int kOffCode = kOffB + 2 * kBBytes;
-constexpr int kOffScale = kOffCode + kStages * kCodeBytes;
-constexpr int kScaleBytes = 256 * 64;  // up to 32 groups x 2 B per row
-constexpr int kOffBias = kOffScale + kScaleBytes;
-constexpr int kOffBar = kOffBias + kScaleBytes;
-constexpr int kGemmSmem = kOffBar + 256 + 1024;  // + alignment slack
+// Work unit = (tile of <= 128 token rows of one expert, two 128-row weight
+// blocks sharing that token tile): gate rows f0..f0+127 and up rows
+// f0..f0+127 for gate/up, output rows f0..f0+255 for down.  Every token row
+// brought on chip feeds 256 weight rows.  Each weight block has its own TMEM
+// accumulator and its own MMA-issuing thread: one tcgen05.mma (M=128, N=tile
+// rows rounded to 16, K=16) has a fixed issue cost, and two issuers keep the
+// tensor pipe fed at N <= 128.
+//
+// Warp roles: 0-7 weight producers (warp w: block w >> 2, TMEM lanes
+// 32 * (w & 3) ...), 8-15 epilogue, 16-17 MMA issue (one thread each; warp 16
+// also allocates TMEM), 18 token loads (one thread issues the TMAs).
+constexpr int kGemmWarps = 19;
+constexpr int kGemmThreads = kGemmWarps * 32;
+constexpr int kMmaWarp = 16;
+constexpr int kLoadWarp = 18;
+constexpr int kEpiThreads = 256;
+constexpr int kTokStages = 8;
+constexpr int kAStages = 4;           // == the producers' register prefetch depth
+constexpr int kTokStageBytes = kTileRows * 128;  // 128 rows x 64 fp16, 128-byte swizzle
+// TMEM columns: acc0 [0,128) | acc1 [128,256) | A stage s at 256 + 64 s (block 0 +0, block 1 +32)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = 256;
+
+struct GemmSync {
+  uint64_t tok_full[kTokStages];
+  uint64_t tok_empty[kTokStages];
+  uint64_t a_full[kAStages];
+  uint64_t a_empty[kAStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint32_t tmem;
+  int col_pos[2][kTileRows];        // down epilogue: output row of each column
+};
+constexpr int kGemmSmem = 1024 + kTokStages * kTokStageBytes + (int)sizeof(GemmSync);
+static_assert(kGemmSmem <= 227 * 1024, "shared memory");
+static_assert(kGemmSmem > 114 * 1024, "one CTA per SM: the kernel allocates all of TMEM");
 
 struct GemmArgs {
+  CUtensorMap map_rows;  // B operand rows: MODE 0 gathered x [P+T][2048], MODE 1 act [P+T][512]; box 64 x 128
   LayerW L;
-  int T;
-  const __half* a_routed;   // MODE 0: x [T][2048]; MODE 1: routed act [T*8][512] (perm order)
-  const __half* a_shared;   // MODE 0: x; MODE 1: shared act [T][512]
   const int* perm;
-  const int* offsets;
-  const int2* tiles;
+  const int4* tiles;
   const int* n_tiles;
-  __half* act_out;          // MODE 0: routed act [T*8][512]
-  __half* act_sh_out;       // MODE 0: shared act [T][512]
-  const float* w;           // MODE 1: routing weights [T*8]
-  float* y_pos;             // MODE 1: [T*8][2048]
-  float* y_sh;              // MODE 1: [T][2048]
+  __half* act;  // MODE 0 output: [P+T][512] (permuted K)
+  float* y;     // MODE 1 output: unweighted [P+T][2048]; routed row = position t*8+k
+  int P;        // routed positions (8T)
   int* status;
 };
 
-// q*s + b for 8 nibbles of one word, written as 8 fp16 in element order
-__device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2, __half2 b2) {
-  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  const __half2 k16inv = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));  // 1/16
-  const __half2 km64 = __halves2half2(__ushort_as_half(0xD400), __ushort_as_half(0xD400));    // -64
-  const uint32_t w8 = w >> 8;
-  uint32_t p0 = (w & 0x000F000Fu) | 0x64006400u;   // 1024 + (e0, e4)
-  uint32_t p1 = (w & 0x00F000F0u) | 0x64006400u;   // 1024 + 16*(e1, e5)
-  uint32_t p2 = (w8 & 0x000F000Fu) | 0x64006400u;  // 1024 + (e2, e6)
-  uint32_t p3 = (w8 & 0x00F000F0u) | 0x64006400u;  // 1024 + 16*(e3, e7)
-  __half2 q0 = __hsub2(*reinterpret_cast<__half2*>(&p0), k1024);
-  __half2 q1 = __hfma2(*reinterpret_cast<__half2*>(&p1), k16inv, km64);
-  __half2 q2 = __hsub2(*reinterpret_cast<__half2*>(&p2), k1024);
-  __half2 q3 = __hfma2(*reinterpret_cast<__half2*>(&p3), k16inv, km64);
-  q0 = __hfma2(q0, s2, b2);
-  q1 = __hfma2(q1, s2, b2);
-  q2 = __hfma2(q2, s2, b2);
-  q3 = __hfma2(q3, s2, b2);
-  const uint32_t r0 = *reinterpret_cast<uint32_t*>(&q0), r1 = *reinterpret_cast<uint32_t*>(&q1);
-  const uint32_t r2 = *reinterpret_cast<uint32_t*>(&q2), r3 = *reinterpret_cast<uint32_t*>(&q3);
-  uint4 o;
-  o.x = __byte_perm(r0, r1, 0x5410);  // e0 e1
-  o.y = __byte_perm(r2, r3, 0x5410);  // e2 e3
-  o.z = __byte_perm(r0, r1, 0x7632);  // e4 e5
-  o.w = __byte_perm(r2, r3, 0x7632);  // e6 e7
-  return o;
+template <bool BF16>
+__device__ __forceinline__ uint32_t half_bits(uint16_t u) {
+  if constexpr (BF16) {
+    return __half_as_ushort(__float2half_rn(__uint_as_float((uint32_t)u << 16)));
+  } else {
+    return u;
+  }
 }
 
-template <bool BF16>
-__device__ __forceinline__ __half to_half(uint16_t u) {
-  if constexpr (BF16) {
-    return __float2half_rn(__uint_as_float((uint32_t)u << 16));
+// 8 nibbles of one word -> 4 fp16 pairs (e0,e4) (e1,e5) (e2,e6) (e3,e7):
+// q exact (1024 + q, or 1024 + 16 q scaled by 1/16), then q*s + b rounded once
+__device__ __forceinline__ void dequant_word(uint32_t w, __half2 s2, __half2 b2, uint32_t* o) {
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 k16inv = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));
+  const __half2 km64 = __halves2half2(__ushort_as_half(0xD400), __ushort_as_half(0xD400));
+  const uint32_t w8 = w >> 8;
+  uint32_t p0 = (w & 0x000F000Fu) | 0x64006400u;
+  uint32_t p1 = (w & 0x00F000F0u) | 0x64006400u;
+  uint32_t p2 = (w8 & 0x000F000Fu) | 0x64006400u;
+  uint32_t p3 = (w8 & 0x00F000F0u) | 0x64006400u;
+  __half2 q0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&p0), k1024), s2, b2);
+  __half2 q1 = __hfma2(__hfma2(*reinterpret_cast<__half2*>(&p1), k16inv, km64), s2, b2);
+  __half2 q2 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&p2), k1024), s2, b2);
+  __half2 q3 = __hfma2(__hfma2(*reinterpret_cast<__half2*>(&p3), k16inv, km64), s2, b2);
+  o[0] = *reinterpret_cast<uint32_t*>(&q0);
+  o[1] = *reinterpret_cast<uint32_t*>(&q1);
+  o[2] = *reinterpret_cast<uint32_t*>(&q2);
+  o[3] = *reinterpret_cast<uint32_t*>(&q3);
+}
+
+struct RowPtrs {
+  const uint8_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+};
+
+template <int MODE>
+struct Geo {
+  static constexpr int K = MODE == 0 ? kHidden : kInter;
+  static constexpr int KS = K / 64;
+  static constexpr int PARTS = MODE == 0 ? kInter / 128 : kHidden / 256;
+};
+
+// the weight row a producer thread streams for unit u (block blk, TMEM lane r)
+template <int MODE>
+__device__ __forceinline__ RowPtrs unit_rows(const GemmArgs& a, int u, int blk, int r) {
+  const int4 t = a.tiles[u / Geo<MODE>::PARTS];
+  const int part = u % Geo<MODE>::PARTS;
+  const uint8_t* rec = t.x == kExperts ? a.L.shared : a.L.bank + (uint64_t)t.x * a.L.stride;
+  RowPtrs p;
+  if (MODE == 0) {
+    const int f = part * 128 + r;
+    p.w = rec + (blk ? kOffUpW : kOffGateW) + (size_t)f * (kHidden / 2);
+    p.s = reinterpret_cast<const uint16_t*>(rec + (blk ? kOffUpS : kOffGateS)) + f * (kHidden / kGroup);
+    p.b = reinterpret_cast<const uint16_t*>(rec + (blk ? kOffUpB : kOffGateB)) + f * (kHidden / kGroup);
   } else {
-    return __ushort_as_half(u);
+    const int f = part * 256 + blk * 128 + r;
+    p.w = rec + kOffDownW + (size_t)f * (kInter / 2);
+    p.s = reinterpret_cast<const uint16_t*>(rec + kOffDownS) + f * (kInter / kGroup);
+    p.b = reinterpret_cast<const uint16_t*>(rec + kOffDownB) + f * (kInter / kGroup);
   }
+  return p;
+}
+
+__device__ __forceinline__ float silu_mul_fast(float g, float u) {
+  const float e = __expf(fminf(-g, 80.0f));
+  return __fdividef(g, 1.0f + e) * u;
 }
 
 template <bool BF16, int MODE>
-__global__ void __launch_bounds__(kGThreads, 1) k_moe_gemm(const __grid_constant__ GemmArgs a) {
-  constexpr int K = MODE == 0 ? kHidden : kInter;
-  constexpr int KS = K / 64;                  // 64-column groups
-  constexpr int NG = K / 64;                  // scale groups per B row
+__global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_constant__ GemmArgs a) {
+  constexpr int KS = Geo<MODE>::KS;
+  constexpr int PARTS = Geo<MODE>::PARTS;
+  static_assert(KS % kAStages == 0, "producer unroll needs KS % kAStages == 0");
   extern __shared__ uint8_t gsm_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* mma_done = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [kStages]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffBar + 128);
+  uint8_t* ring =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  GemmSync* sy = reinterpret_cast<GemmSync*>(ring + kTokStages * kTokStageBytes);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if ((int)blockIdx.x >= *a.n_tiles) return;
-  const int2 tile = a.tiles[blockIdx.x];
-  const int e = tile.x, m0 = tile.y;
-  const bool shared = (e == kExperts);
-  const int row_base = shared ? 0 : a.offsets[e];
-  const int n_e = shared ? a.T : (a.offsets[e + 1] - a.offsets[e]);
-  const int nrows = min(128, n_e - m0);
-  const uint8_t* rec = shared ? a.L.shared : a.L.bank + (uint64_t)e * a.L.stride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_units = *a.n_tiles * PARTS;
+  const int G = gridDim.x;
+  if ((int)blockIdx.x >= n_units) return;
+  const int my_units = (n_units - (int)blockIdx.x + G - 1) / G;
 
-  // B rows of this N tile: MODE 0 rows 0..127 gate features f0.., 128..255 up
-  // features f0..; MODE 1 rows = output features n0..n0+255.
-  const int f0 = MODE == 0 ? blockIdx.y * 128 : blockIdx.y * 256;
-
-  // scales and biases of the 256 B rows, all groups (one copy per CTA)
-  {
-    uint8_t* ss = sm + kOffScale;
-    uint8_t* bb = sm + kOffBias;
-    constexpr int rowb = NG * 2;            // bytes per row
-    constexpr int chunks = rowb / 16;       // 16-byte chunks per row
-    for (int c = tid; c < 256 * chunks; c += kGThreads) {
-      const int r = c / chunks, q = c % chunks;
-      size_t so, bo;
-      if (MODE == 0) {
-        const int f = f0 + (r & 127);
-        so = (r < 128 ? kOffGateS : kOffUpS) + (size_t)f * rowb;
-        bo = (r < 128 ? kOffGateB : kOffUpB) + (size_t)f * rowb;
-      } else {
-        so = kOffDownS + (size_t)(f0 + r) * rowb;
-        bo = kOffDownB + (size_t)(f0 + r) * rowb;
-      }
-      cp16(ss + r * rowb + q * 16, rec + so + q * 16, 16);
-      cp16(bb + r * rowb + q * 16, rec + bo + q * 16, 16);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTokStages; s++) {
+      mbar_init(&sy->tok_full[s], 1);
+      mbar_init(&sy->tok_empty[s], 2);
     }
-    cp_commit();
-  }
-
-  // per-thread A-row sources for the gather: 4 chunks per thread per stage
-  // (row = (tid >> 3) + 32 * j, chunk = tid & 7)
-  const int a_chunk = tid & 7;
-  const __half* a_src[4];
-  uint32_t a_bytes[4];
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const int i = (tid >> 3) + 32 * j;
-    if (i < nrows) {
-      const int p = row_base + m0 + i;
-      if (MODE == 0) {
-        const int tok = shared ? p : (a.perm[p] >> 3);
-        a_src[j] = a.a_routed + (size_t)tok * kHidden + a_chunk * 8;
-      } else {
-        a_src[j] = (shared ? a.a_shared : a.a_routed) + (size_t)p * kInter + a_chunk * 8;
-      }
-      a_bytes[j] = 16;
-    } else {
-      a_src[j] = MODE == 0 ? a.a_routed : (shared ? a.a_shared : a.a_routed);
-      a_bytes[j] = 0;  // zero fill
+    for (int s = 0; s < kAStages; s++) {
+      mbar_init(&sy->a_full[s], 8);
+      mbar_init(&sy->a_empty[s], 2);
     }
-  }
-  // code sources: 2 chunks per thread per stage (row = tid, halves 0/1 of its 32 bytes)
-  const uint8_t* c_src;
-  {
-    const int r = tid;
-    size_t off;
-    if (MODE == 0) {
-      const int f = f0 + (r & 127);
-      off = (r < 128 ? kOffGateW : kOffUpW) + (size_t)f * (kHidden / 2);
-    } else {
-      off = kOffDownW + (size_t)(f0 + r) * (kInter / 2);
-    }
-    c_src = rec + off;
-  }
-  auto issue = [&](int ks) {
-    const int st = ks % kStages;
-    uint8_t* A = sm + kOffA + st * kABytes;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int i = (tid >> 3) + 32 * j;
-      cp16(A + sw128(i, a_chunk), a_src[j] + ks * 64, a_bytes[j]);
-    }
-    uint8_t* Cd = sm + kOffCode + st * kCodeBytes;
-    cp16(Cd + tid * 32, c_src + ks * 32, 16);
-    cp16(Cd + tid * 32 + 16, c_src + ks * 32 + 16, 16);
-    cp_commit();
-  };
-
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(s_u32(tmem_slot)));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  if (tid == 0) {
-    for (int s = 0; s < kStages; s++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&mma_done[s])));
+    mbar_init(&sy->acc_full, 2);
+    mbar_init(&sy->acc_empty, 8);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  for (int ks = 0; ks < kStages - 1 && ks < KS; ks++) issue(ks);
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(&sy->tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
   __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t idesc = (1u << 4) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
+  tc_fence_after();
+  const uint32_t tmem = sy->tmem;
   bool ok = true;
 
-  for (int ks = 0; ks < KS; ks++) {
-    // this thread's copies for step ks have landed (the group count allows the
-    // later steps, plus the scale group on the first step, to stay in flight)
-    if (ks + kStages - 1 <= KS) cp_wait<kStages - 2>(); else cp_wait<0>();
-    __syncthreads();
-    // dequant the codes of step ks into B[ks & 1]
-    {
-      const uint8_t* Cd = sm + kOffCode + (ks % kStages) * kCodeBytes;
-      uint8_t* B = sm + kOffB + (ks & 1) * kBBytes;
-      const uint16_t* ss = reinterpret_cast<const uint16_t*>(sm + kOffScale);
-      const uint16_t* bb = reinterpret_cast<const uint16_t*>(sm + kOffBias);
-      for (int wdx = tid; wdx < 256 * 8; wdx += kGThreads) {
-        const int r = wdx >> 3, c = wdx & 7;
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(Cd + r * 32 + c * 4);
-        const __half s = to_half<BF16>(ss[r * NG + ks]);
-        const __half b = to_half<BF16>(bb[r * NG + ks]);
-        *reinterpret_cast<uint4*>(B + sw128(r, c)) = dequant8(w, __halves2half2(s, s), __halves2half2(b, b));
+  if (warp < 8) {
+    // ---------------- weight producers: Q4 -> fp16 -> TMEM (A operand)
+    const int q = warp & 3, blk = warp >> 2, r = q * 32 + lane;
+    const int total = my_units * KS;
+    uint32_t cw[kAStages][8];
+    uint32_t sb[kAStages];
+    int pu = 0, pks = 0;
+    RowPtrs pc = unit_rows<MODE>(a, blockIdx.x, blk, r);
+    auto fetch = [&](uint32_t(&dst)[8], uint32_t& dsb) {
+      ld_codes32(pc.w + pks * 32, dst);
+      dsb = (uint32_t)__ldg(pc.s + pks) | ((uint32_t)__ldg(pc.b + pks) << 16);
+      if (++pks == KS) {
+        pks = 0;
+        if (++pu < my_units) pc = unit_rows<MODE>(a, blockIdx.x + pu * G, blk, r);
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < kAStages; j++) fetch(cw[j], sb[j]);
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + kTmemA + blk * 32;
+    for (int g = 0; g < total; g += kAStages) {
+#pragma unroll
+      for (int j = 0; j < kAStages; j++) {
+        const int flat = g + j;
+        const uint32_t sbits = half_bits<BF16>(sb[j] & 0xFFFFu), bbits = half_bits<BF16>(sb[j] >> 16);
+        const __half2 s2 = __halves2half2(__ushort_as_half(sbits), __ushort_as_half(sbits));
+        const __half2 b2 = __halves2half2(__ushort_as_half(bbits), __ushort_as_half(bbits));
+        uint32_t o[32];
+#pragma unroll
+        for (int wi = 0; wi < 8; wi++) dequant_word(cw[j][wi], s2, b2, o + 4 * wi);
+        if (flat + kAStages < total) fetch(cw[j], sb[j]);
+        if (!mbar_wait(&sy->a_empty[j], ((flat / kAStages) & 1) ^ 1)) ok = false;
+        tc_fence_after();
+        tmem_st32(tbase + j * 64, o);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sy->a_full[j]);
       }
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t abase = s_u32(sm + kOffA + (ks % kStages) * kABytes);
-      const uint32_t bbase = s_u32(sm + kOffB + (ks & 1) * kBBytes);
-#pragma unroll
-      for (int kk = 0; kk < 4; kk++) {
-        const uint64_t da = sdesc(abase + kk * 32);
-        const uint64_t db = sdesc(bbase + kk * 32);
-        const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-        asm volatile(
-            "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
-                tmem),
-            "l"(da), "l"(db), "r"(idesc), "r"(accum));
+  } else if (warp < 16) {
+    // ---------------- epilogue: TMEM -> SiLU(g)*u fp16 act / weighted fp32 y
+    const int eq = warp & 3, half = (warp - 8) >> 2, et = threadIdx.x - 256;
+    const uint32_t lrow = (uint32_t)(eq * 32) << 16;
+    for (int i = 0; i < my_units; i++) {
+      const int u = blockIdx.x + i * G;
+      const int4 t = a.tiles[u / PARTS];
+      const int part = u % PARTS;
+      const bool shared = t.x == kExperts;
+      const int n = t.z;
+      const int pb = t.w + t.y;  // first row of the tile in the row space
+      if (MODE == 1) {
+        for (int c = et; c < n; c += kEpiThreads) sy->col_pos[i & 1][c] = shared ? pb + c : a.perm[pb + c];
+        named_sync(2, kEpiThreads);
       }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       s_u32(&mma_done[ks % kStages]))
-                   : "memory");
-    }
-    // MMA(ks-1) must be done before its A stage is refilled (with step
-    // ks + kStages - 1) and before B[(ks+1) & 1] is overwritten
-    if (ks >= 1) {
-      const int pk = ks - 1;
-      if (!mbar_wait_p(&mma_done[pk % kStages], (pk / kStages) & 1)) ok = false;
-    }
-    if (ks + kStages - 1 < KS) issue(ks + kStages - 1);
-  }
-  // all MMAs complete (in order) once the last one is
-  if (!mbar_wait_p(&mma_done[(KS - 1) % kStages], ((KS - 1) / kStages) & 1)) ok = false;
-  if (!ok) set_status(a.status, kStatusTimeout);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-
-  // ---- epilogue: TMEM lane = tile row; warps w and w+4 split the columns
-  const int i = (warp & 3) * 32 + lane;
-  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-  if (MODE == 0) {
-    const int cbeg = (warp >> 2) * 64;
-    __half* dst = nullptr;
-    if (i < nrows) {
-      const int p = row_base + m0 + i;
-      dst = shared ? a.act_sh_out + (size_t)p * kInter : a.act_out + (size_t)p * kInter;
-    }
-    for (int c = cbeg; c < cbeg + 64; c += 16) {
-      uint32_t g[16], u[16];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(g[0]), "=r"(g[1]), "=r"(g[2]), "=r"(g[3]), "=r"(g[4]), "=r"(g[5]), "=r"(g[6]), "=r"(g[7]),
-            "=r"(g[8]), "=r"(g[9]), "=r"(g[10]), "=r"(g[11]), "=r"(g[12]), "=r"(g[13]), "=r"(g[14]), "=r"(g[15])
-          : "r"(lane_addr + c));
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
-            "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15])
-          : "r"(lane_addr + 128 + c));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (dst) {
-        uint32_t h[8];
+      if (!mbar_wait(&sy->acc_full, i & 1)) ok = false;
+      tc_fence_after();
+      const int cbeg = half * (kTileRows / 2), cend = min(n, cbeg + kTileRows / 2);
+      if (MODE == 0) {
+        const int f = part * 128 + eq * 32 + lane;
+        const int fp = (f & ~7) | ((f & 3) << 1) | ((f >> 2) & 1);
+        __half* dst = a.act + (size_t)pb * kInter + fp;
+        for (int c0 = cbeg; c0 < cend; c0 += 16) {
+          uint32_t g[16], v[16];
+          tmem_ld16(tmem + lrow + c0, g);
+          tmem_ld16(tmem + lrow + 128 + c0, v);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const float a0 = silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]));
-          const float a1 = silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]));
-          const __half2 hv = __floats2half2_rn(a0, a1);
-          h[j] = *reinterpret_cast<const uint32_t*>(&hv);
+          for (int j = 0; j < 16; j++)
+            if (c0 + j < cend)
+              dst[(size_t)(c0 + j) * kInter] =
+                  __float2half_rn(silu_mul_fast(__uint_as_float(g[j]), __uint_as_float(v[j])));
         }
-        uint4* d4 = reinterpret_cast<uint4*>(dst + f0 + c);
-        d4[0] = make_uint4(h[0], h[1], h[2], h[3]);
-        d4[1] = make_uint4(h[4], h[5], h[6], h[7]);
-      }
-    }
-  } else {
-    const int cbeg = (warp >> 2) * 128;
-    float* dst = nullptr;
-    float wgt = 1.f;
-    if (i < nrows) {
-      const int p = row_base + m0 + i;
-      if (shared) {
-        dst = a.y_sh + (size_t)p * kHidden;
       } else {
-        const int pos = a.perm[p];
-        dst = a.y_pos + (size_t)pos * kHidden;
-        wgt = a.w[pos];
+        const int f = part * 256 + eq * 32 + lane;
+        float* base = a.y + f;
+        for (int c0 = cbeg; c0 < cend; c0 += 32) {
+          uint32_t v0[32], v1[32];
+          tmem_ld32(tmem + lrow + c0, v0);
+          tmem_ld32(tmem + lrow + 128 + c0, v1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (c0 + j < cend) {
+              float* d = base + (size_t)sy->col_pos[i & 1][c0 + j] * kHidden;
+              d[0] = __uint_as_float(v0[j]);
+              d[128] = __uint_as_float(v1[j]);
+            }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sy->acc_empty);
+    }
+  } else if (warp < kLoadWarp) {
+    // ---------------- MMA issue: warp 16 -> block 0 / acc0, warp 17 -> block 1 / acc1
+    if (lane == 0) {
+      const uint32_t blk = (uint32_t)(warp - kMmaWarp);
+      const uint32_t dacc = tmem + blk * 128;
+      int gs = 0;
+      for (int i = 0; i < my_units; i++) {
+        const int u = blockIdx.x + i * G;
+        const uint32_t N = (uint32_t)((a.tiles[u / PARTS].z + 15) & ~15);
+        const uint32_t idesc = (1u << 4) | ((N >> 3) << 17) | ((128u >> 4) << 24);
+        if (!mbar_wait(&sy->acc_empty, (i & 1) ^ 1)) ok = false;
+        tc_fence_after();
+        for (int ks = 0; ks < KS; ks++, gs++) {
+          const int ts = gs % kTokStages, as = gs % kAStages;
+          if (!mbar_wait(&sy->tok_full[ts], (gs / kTokStages) & 1)) ok = false;
+          if (!mbar_wait(&sy->a_full[as], (gs / kAStages) & 1)) ok = false;
+          tc_fence_after();
+          const uint32_t bb = s_u32(ring + ts * kTokStageBytes);
+          const uint32_t ac = tmem + kTmemA + as * 64 + blk * 32;
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++) mma_ts(dacc, ac + kk * 8, sdesc(bb + kk * 32), idesc, (ks | kk) ? 1u : 0u);
+          tc_commit(&sy->tok_empty[ts]);
+          tc_commit(&sy->a_empty[as]);
+        }
+        tc_commit(&sy->acc_full);
       }
     }
-    for (int c = cbeg; c < cbeg + 128; c += 16) {
-      uint32_t v[16];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-          : "r"(lane_addr + c));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (dst) {
-        float4* d4 = reinterpret_cast<float4*>(dst + f0 + c);
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          d4[j] = make_float4(__fmul_rn(__uint_as_float(v[4 * j]), wgt), __fmul_rn(__uint_as_float(v[4 * j + 1]), wgt),
-                              __fmul_rn(__uint_as_float(v[4 * j + 2]), wgt), __fmul_rn(__uint_as_float(v[4 * j + 3]), wgt));
+  } else if (lane == 0) {
+    // ---------------- token rows by TMA: one 2-D tile (64 columns x 128 rows) per step
+    int gs = 0;
+    for (int i = 0; i < my_units; i++) {
+      const int u = blockIdx.x + i * G;
+      const int4 t = a.tiles[u / PARTS];
+      const int pb = t.w + t.y;
+      for (int ks = 0; ks < KS; ks++, gs++) {
+        const int ts = gs % kTokStages;
+        if (!mbar_wait(&sy->tok_empty[ts], ((gs / kTokStages) & 1) ^ 1)) ok = false;
+        mbar_expect_tx(&sy->tok_full[ts], kTokStageBytes);
+        tma_tile(ring + ts * kTokStageBytes, &a.map_rows, ks * 64, pb, &sy->tok_full[ts]);
       }
     }
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+
+  if (!ok) set_status(a.status, kStatusTimeout);
+  tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
 }
 
-// out = (residual + sigmoid(c) * shared) + sum_k y_k, the y rows already
-// weighted by the routing weight (router order, deltanet.metal:2213-2227)
+// out = (residual + sigmoid(c) * shared) + sum_k w_k * y_k, the products
+// rounded and summed in router order (deltanet.metal:2213-2227)
 __global__ void __launch_bounds__(256) k_combine_weighted(int T, const float* __restrict__ residual,
                                                           const float* __restrict__ y_pos,
+                                                          const float* __restrict__ w,
                                                           const float* __restrict__ y_sh,
                                                           const float* __restrict__ coef,
                                                           float* __restrict__ out) {
   const int t = blockIdx.x;
   const float c = coef[t];
   const float coeff = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-c)));
-  for (int r = threadIdx.x; r < kHidden; r += 256) {
-    const float sh = __fmul_rn(y_sh[(size_t)t * kHidden + r], coeff);
-    float routed = y_pos[(size_t)(t * kTopK) * kHidden + r];
+  float wk[kTopK];
 #pragma unroll
-    for (int k = 1; k < kTopK; k++) routed = __fadd_rn(routed, y_pos[(size_t)(t * kTopK + k) * kHidden + r]);
-    const float base = residual ? residual[(size_t)t * kHidden + r] : 0.f;
-    out[(size_t)t * kHidden + r] = __fadd_rn(__fadd_rn(base, sh), routed);
+  for (int k = 0; k < kTopK; k++) wk[k] = w[t * kTopK + k];
+  const float4* y4 = reinterpret_cast<const float4*>(y_pos + (size_t)t * kTopK * kHidden);
+  const float4* s4 = reinterpret_cast<const float4*>(y_sh + (size_t)t * kHidden);
+  const float4* r4 = residual ? reinterpret_cast<const float4*>(residual + (size_t)t * kHidden) : nullptr;
+  float4* o4 = reinterpret_cast<float4*>(out + (size_t)t * kHidden);
+  for (int i = threadIdx.x; i < kHidden / 4; i += 256) {
+    float4 y = y4[i];
+    float4 acc = make_float4(__fmul_rn(y.x, wk[0]), __fmul_rn(y.y, wk[0]), __fmul_rn(y.z, wk[0]), __fmul_rn(y.w, wk[0]));
+#pragma unroll
+    for (int k = 1; k < kTopK; k++) {
+      y = y4[k * (kHidden / 4) + i];
+      acc.x = __fadd_rn(acc.x, __fmul_rn(y.x, wk[k]));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(y.y, wk[k]));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(y.z, wk[k]));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(y.w, wk[k]));
+    }
+    const float4 sh = s4[i];
+    const float4 base = r4 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    o4[i] = make_float4(__fadd_rn(__fadd_rn(base.x, __fmul_rn(sh.x, coeff)), acc.x),
+                        __fadd_rn(__fadd_rn(base.y, __fmul_rn(sh.y, coeff)), acc.y),
+                        __fadd_rn(__fadd_rn(base.z, __fmul_rn(sh.z, coeff)), acc.z),
+                        __fadd_rn(__fadd_rn(base.w, __fmul_rn(sh.w, coeff)), acc.w));
   }
 }
 
@@ -509,9 +664,13 @@ __global__ void __launch_bounds__(256) k_combine_weighted(int T, const float* __
 // ------------------------------------------------------------------ host side
 static size_t al256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
+static size_t max_tiles_for(int T) {
+  return static_cast<size_t>(T) * kTopK / kTileRows + kExperts + (T + kTileRows - 1) / kTileRows + 1;
+}
+
 size_t prefill_workspace_bytes(int T) {
   const size_t P = static_cast<size_t>(T) * kTopK;
-  const size_t max_tiles = P / 128 + kExperts + (T + 127) / 128 + 1;
+  const size_t R = P + static_cast<size_t>(T);  // row space: routed positions + shared tokens
   size_t b = 0;
   b += al256(4 * (size_t)T * kExperts);          // logits
   b += al256(4 * (size_t)T);                     // coef
@@ -519,27 +678,54 @@ size_t prefill_workspace_bytes(int T) {
   b += al256(4 * (kExperts + 1)) * 2;            // counts, offsets
   b += al256(4 * P);                             // perm
   b += al256(dispatch_workspace_bytes(T));       // plan scratch
-  b += al256(8 * max_tiles) + al256(16);         // tiles, count
-  b += al256(2 * P * kInter);                    // routed act (fp16)
-  b += al256(2 * (size_t)T * kInter);            // shared act (fp16)
-  b += al256(4 * P * kHidden);                   // y per position
-  b += al256(4 * (size_t)T * kHidden);           // shared y
+  b += al256(16 * max_tiles_for(T)) + al256(16); // tiles, count
+  b += al256(2 * R * kHidden);                   // gathered x (fp16, permuted K)
+  b += al256(2 * R * kInter);                    // act (fp16, permuted K)
+  b += al256(4 * R * kHidden);                   // y (fp32)
   return b;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+static PFN_cuTensorMapEncodeTiled encode_fn() {
+  static PFN_cuTensorMapEncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+  }
+  return fn;
+}
+
+// fp16 matrix [rows][cols] (row-major), box = 64 columns (128 bytes) x box_rows,
+// 128-byte swizzle: the K-major operand layout the MMA descriptors expect
+static bool encode_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t prefill_init_attributes() {
+  if (!encode_fn()) return cudaErrorNotSupported;
   cudaError_t e;
   e = cudaFuncSetAttribute(k_router_prefill<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_router_prefill<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_moe_gemm<false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  e = cudaFuncSetAttribute(k_grouped<false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_moe_gemm<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  e = cudaFuncSetAttribute(k_grouped<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_moe_gemm<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  e = cudaFuncSetAttribute(k_grouped<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(k_moe_gemm<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  return cudaFuncSetAttribute(k_grouped<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
 }
 
 cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
@@ -555,9 +741,9 @@ cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, i
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
                           float* w_out, void* workspace, int* status, Prof* prof) {
-  (void)prof;
   const size_t P = static_cast<size_t>(T) * kTopK;
-  const size_t max_tiles = P / 128 + kExperts + (T + 127) / 128 + 1;
+  const size_t R = P + static_cast<size_t>(T);
+  const size_t max_tiles = max_tiles_for(T);
   char* p = static_cast<char*>(workspace);
   auto take = [&](size_t n) {
     char* q = p;
@@ -572,20 +758,31 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   int* offsets = reinterpret_cast<int*>(take(4 * (kExperts + 1)));
   int* perm = reinterpret_cast<int*>(take(4 * P));
   int* plan_ws = reinterpret_cast<int*>(take(dispatch_workspace_bytes(T)));
-  int2* tiles = reinterpret_cast<int2*>(take(8 * max_tiles));
+  int4* tiles = reinterpret_cast<int4*>(take(16 * max_tiles));
   int* n_tiles = reinterpret_cast<int*>(take(16));
-  __half* act = reinterpret_cast<__half*>(take(2 * P * kInter));
-  __half* act_sh = reinterpret_cast<__half*>(take(2 * (size_t)T * kInter));
-  float* y_pos = reinterpret_cast<float*>(take(4 * P * kHidden));
-  float* y_sh = reinterpret_cast<float*>(take(4 * (size_t)T * kHidden));
+  uint16_t* xs = reinterpret_cast<uint16_t*>(take(2 * R * kHidden));
+  __half* act = reinterpret_cast<__half*>(take(2 * R * kInter));
+  float* y = reinterpret_cast<float*>(take(4 * R * kHidden));
 
-  cudaError_t e = router_logits_prefill(st, L, bf16, T, x, logits, coef);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  GemmArgs g0, g1;
+  if (!encode_rows(&g0.map_rows, xs, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows))
+    return cudaErrorInvalidValue;
+
+  {
+    ProfScope ps(prof, kKRouter, st);
+    e = router_logits_prefill(st, L, bf16, T, x, logits, coef);
+  }
   if (e != cudaSuccess) return e;
   if (r.idx_in) {
     e = cudaMemcpyAsync(idx, r.idx_in, 4 * P, cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return e;
     e = cudaMemcpyAsync(w, r.w_in, 4 * P, cudaMemcpyDeviceToDevice, st);
   } else {
+    ProfScope ps(prof, kKTopk, st);
     e = router_topk(st, T, logits, r.bias, idx, w, status);
   }
   if (e != cudaSuccess) return e;
@@ -594,36 +791,38 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   if (e != cudaSuccess) return e;
   e = dispatch_plan_ws(st, idx, T, counts, offsets, perm, plan_ws, status);
   if (e != cudaSuccess) return e;
-  k_tile_map<<<1, 32, 0, st>>>(counts, T, tiles, n_tiles);
+  k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, tiles, n_tiles);
+  k_gather_rows<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(perm, (int)P, T, reinterpret_cast<const uint4*>(x),
+                                                          reinterpret_cast<uint4*>(xs));
 
-  GemmArgs ga;
-  ga.L = L;
-  ga.T = T;
-  ga.a_routed = reinterpret_cast<const __half*>(x);
-  ga.a_shared = reinterpret_cast<const __half*>(x);
-  ga.perm = perm;
-  ga.offsets = offsets;
-  ga.tiles = tiles;
-  ga.n_tiles = n_tiles;
-  ga.act_out = act;
-  ga.act_sh_out = act_sh;
-  ga.w = w;
-  ga.y_pos = y_pos;
-  ga.y_sh = y_sh;
-  ga.status = status;
-  const dim3 g1((unsigned)max_tiles, kInter / 128);
-  if (bf16)
-    k_moe_gemm<true, 0><<<g1, kGThreads, kGemmSmem, st>>>(ga);
-  else
-    k_moe_gemm<false, 0><<<g1, kGThreads, kGemmSmem, st>>>(ga);
-  ga.a_routed = act;
-  ga.a_shared = act_sh;
-  const dim3 g2((unsigned)max_tiles, kHidden / 256);
-  if (bf16)
-    k_moe_gemm<true, 1><<<g2, kGThreads, kGemmSmem, st>>>(ga);
-  else
-    k_moe_gemm<false, 1><<<g2, kGThreads, kGemmSmem, st>>>(ga);
-  k_combine_weighted<<<T, 256, 0, st>>>(T, residual, y_pos, y_sh, coef, out);
+  g0.L = g1.L = L;
+  g0.perm = g1.perm = perm;
+  g0.tiles = g1.tiles = tiles;
+  g0.n_tiles = g1.n_tiles = n_tiles;
+  g0.act = g1.act = act;
+  g0.y = g1.y = y;
+  g0.P = g1.P = (int)P;
+  g0.status = g1.status = status;
+  const unsigned grid0 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<0>::PARTS);
+  {
+    ProfScope ps(prof, kKGateUp, st);
+    if (bf16)
+      k_grouped<true, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
+    else
+      k_grouped<false, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
+  }
+  const unsigned grid1 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<1>::PARTS);
+  {
+    ProfScope ps(prof, kKDown, st);
+    if (bf16)
+      k_grouped<true, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
+    else
+      k_grouped<false, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
+  }
+  {
+    ProfScope ps(prof, kKCombine, st);
+    k_combine_weighted<<<T, 256, 0, st>>>(T, residual, y, w, y + P * kHidden, coef, out);
+  }
   return cudaGetLastError();
 }
 

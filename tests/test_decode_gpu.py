@@ -222,9 +222,22 @@ def test_bad_record_is_reported_not_faulted(ctx, layers):
 
 
 def test_argument_errors(ctx, layers):
-    from qfmoe import QfError, block_forward
-    with pytest.raises(QfError, match="QF_ERR_ARG"):
-        block_forward(ctx, layers[(0, False)], hidden(65).cuda())
+    import ctypes as C
+    from qfmoe._lib import lib
+    x = hidden(8).cuda()
+    out = torch.empty((8, 2048), device="cuda")
+    ws = ctx.workspace(8)
+    d = layers[(0, False)].desc()
+    f = lib().qf_moe_block_forward
+    args = (x.data_ptr(), None, out.data_ptr(), None, None, None, ws.data_ptr(), ws.numel())
+    assert f(ctx.h, C.byref(d), 40000, *args) == -1  # T above the prefill limit
+    assert f(ctx.h, C.byref(d), 0, *args) == -1
+    d.expert_bank += 16  # records are read 32 bytes at a time
+    assert f(ctx.h, C.byref(d), 8, *args) == -1
+    d = layers[(0, False)].desc()
+    d.record_stride += 16
+    assert f(ctx.h, C.byref(d), 8, *args) == -1
+    torch.cuda.synchronize()
 
 
 def test_dispatch_plan_matches_oracle(ctx):

@@ -56,6 +56,9 @@ def _declare(L):
     L.qfo_synth_coef.argtypes = [_u64, C.c_uint32, _i, _p, _p, _p]
     L.qfo_synth_hidden.argtypes = [_u64, _u64, _i, _p]
     L.qfo_topk.argtypes = [_p, _p, _i, _i, _p, _p]
+    L.qfo_router_logits.argtypes = [_p, _p, _p]
+    L.qfo_coef.argtypes = [_p, _p]
+    L.qfo_coef.restype = C.c_float
     L.qfo_block.argtypes = [_p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i]
     L.qfo_rmsnorm_to_f16.argtypes = [_p, _i, C.c_float, _p]
     L.qfo_dispatch_plan.argtypes = [_p, _i, _i, _i, _p, _p, _p]
@@ -168,6 +171,20 @@ def block(layer: OracleLayer, x16: np.ndarray, residual=None, bias=None, idx_in=
     lib().qfo_block(C.byref(layer.c), T, _ptr(x16), _ptr(res), _ptr(b), _ptr(ii), _ptr(wi),
                     _ptr(out), _ptr(idx), _ptr(w), _ptr(logits), _ptr(coef), threads)
     return {"out": out, "idx": idx, "w": w, "logits": logits, "coef": coef}
+
+
+def router(layer: OracleLayer, x16: np.ndarray):
+    """(logits [T, 256], coef [T]) of fp16 bits x16 [T, 2048]: the router rows in the
+    reference lane order (qfo_router_logits) and the shared-gate chain (qfo_coef)."""
+    x = np.ascontiguousarray(x16, np.uint16).reshape(-1, HIDDEN).view(np.float16).astype(np.float32)
+    T = x.shape[0]
+    logits = np.empty((T, EXPERTS), np.float32)
+    coef = np.empty(T, np.float32)
+    L = lib()
+    for t in range(T):
+        L.qfo_router_logits(C.byref(layer.c), _ptr(x[t]), _ptr(logits[t]))
+        coef[t] = L.qfo_coef(C.byref(layer.c), _ptr(x[t]))
+    return logits, coef
 
 
 def topk(logits: np.ndarray, k: int = TOPK, bias=None):

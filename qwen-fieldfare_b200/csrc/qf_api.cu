@@ -184,8 +184,10 @@ qf_status qf_router_logits_q8(qf_moe* h, const qf_moe_layer* layer, int32_t T, c
   if (T < 1 || T > 65536) return fail(h, QF_ERR_ARG, "T must be in [1, 65536]");
   if (!x || !logits || !aligned(x, 16)) return fail(h, QF_ERR_ARG, "x (16-B aligned) and logits are required");
   DeviceGuard g(h->device);
-  cudaError_t e = qf::router_logits(stream_of(h), w, h->dims.scale_dtype == QF_SCALE_BF16, T, x,
-                                    logits, coef, h->d_status);
+  const bool bf16 = h->dims.scale_dtype == QF_SCALE_BF16;
+  cudaError_t e = T > qf::kDecodeMaxTokens
+                      ? qf::router_logits_prefill(stream_of(h), w, bf16, T, x, logits, coef)
+                      : qf::router_logits(stream_of(h), w, bf16, T, x, logits, coef, h->d_status);
   return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_router_logits_q8");
 }
 

@@ -143,6 +143,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+template <bool BF16>
+__device__ __forceinline__ float h16_to_f32(uint16_t u) {
+  if constexpr (BF16) {
+    return __uint_as_float(static_cast<uint32_t>(u) << 16);
+  } else {
+    return __half2float(__ushort_as_half(u));
+  }
+}
+
 // (x0..x7) -> (x0,x4,x1,x5,x2,x6,x3,x7): the K order of the GEMM operands
 __device__ __forceinline__ uint4 permute8(uint4 v) {
   return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
@@ -150,99 +159,150 @@ __device__ __forceinline__ uint4 permute8(uint4 v) {
 }
 
 // ------------------------------------------------------------------ router
-// CTA = 16 tokens (fp32 x in shared memory) x all 256 router rows + the
-// shared-gate coefficient; warp w owns rows w, w+16, ...  Same per-lane order
-// as the decode router (deltanet.metal:2229-2260), xor-butterfly reduction.
-constexpr int kRtTok = 16;
-constexpr int kRtThreads = 512;
+// Logits in the reference lane order (deltanet.metal:2229-2260): lane l of a
+// warp owns bytes blk*256 + l*8 .. +7 of each of the 8 blocks of 256 and
+// accumulates dot = fma-chain of 8 products, acc = fma(s, dot, acc),
+// acc = fma(b, xsum, acc); the lanes are then summed with the xor butterfly
+// 16, 8, 4, 2, 1 (simd_sum), so the logits are bit-identical to the decode
+// router and the oracle.  Each warp carries 2 router rows x 8 tokens at once:
+// every x value a lane reads from shared memory feeds 2 rows, and each row's
+// codes are read as 256 contiguous bytes per block.  In shared memory the two
+// 16-byte halves of 8-element group c are swapped when bit 2 of c is set, so
+// the eight lanes of a quarter-warp (32 bytes apart) read distinct banks.  An extra warp computes
+// the shared-gate coefficient per token as the reference's single sequential
+// chain (qwen_gemv_q8_affine, deltanet.metal:863-902).
+constexpr int kRtTok = 8;
+constexpr int kRtWarps = 8;
+constexpr int kRtRowsPerWarp = 2;
+constexpr int kRtRows = kRtWarps * kRtRowsPerWarp;  // 32 router rows per CTA
+constexpr int kRtThreads = (kRtWarps + 1) * 32;
 constexpr size_t kRtSmem = sizeof(float) * (kRtTok * kHidden + kRtTok * 256);
 
 template <bool BF16>
-__global__ void __launch_bounds__(kRtThreads) k_router_prefill(LayerW L, int T,
-                                                               const uint16_t* __restrict__ x,
-                                                               float* __restrict__ logits,
-                                                               float* __restrict__ coef) {
-  extern __shared__ __align__(16) float rsm[];
-  float* xs = rsm;                       // [16][2048]
-  float* xsum = rsm + kRtTok * kHidden;  // [16][8 blk][32 lane]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kRtThreads, 3) k_router_prefill(LayerW L, int T,
+                                                                  const uint16_t* __restrict__ x,
+                                                                  float* __restrict__ logits,
+                                                                  float* __restrict__ coef) {
+  extern __shared__ float4 rsm4[];
+  float* xs = reinterpret_cast<float*>(rsm4);  // [8][2048]
+  float* xsum = xs + kRtTok * kHidden;         // [8][8 blk][32 lanes]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * kRtTok;
   const int tn = min(kRtTok, T - t0);
-  for (int i = threadIdx.x; i < tn * (kHidden / 8); i += kRtThreads) {
+  for (int i = tid; i < kRtTok * (kHidden / 8); i += kRtThreads) {
     const int t = i / (kHidden / 8), c = i % (kHidden / 8);
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
-    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (t < tn) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+      const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), cc = __half22float2(h[2]),
+                   dd = __half22float2(h[3]);
+      lo = make_float4(a.x, a.y, b.x, b.y);
+      hi = make_float4(cc.x, cc.y, dd.x, dd.y);
+    }
     float4* d = reinterpret_cast<float4*>(xs + t * kHidden + c * 8);
-    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), cc = __half22float2(h[2]),
-                 dd = __half22float2(h[3]);
-    d[0] = make_float4(a.x, a.y, b.x, b.y);
-    d[1] = make_float4(cc.x, cc.y, dd.x, dd.y);
+    const int sw = (c >> 2) & 1;
+    d[sw] = lo;
+    d[sw ^ 1] = hi;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < tn * 256; i += kRtThreads) {
-    const float* e = xs + (i >> 8) * kHidden + ((i >> 5) & 7) * 256 + (i & 31) * 8;
-    float s = e[0];
-#pragma unroll
-    for (int j = 1; j < 8; j++) s = __fadd_rn(s, e[j]);
-    xsum[i] = s;
+  for (int i = tid; i < kRtTok * 256; i += kRtThreads) {
+    const int c = i & 255;  // 8-element group within the token row
+    const float4* e = reinterpret_cast<const float4*>(xs + (i >> 8) * kHidden + c * 8);
+    const int sw = (c >> 2) & 1;
+    const float4 lo = e[sw], hi = e[sw ^ 1];
+    float v = lo.x;
+    v = __fadd_rn(v, lo.y);
+    v = __fadd_rn(v, lo.z);
+    v = __fadd_rn(v, lo.w);
+    v = __fadd_rn(v, hi.x);
+    v = __fadd_rn(v, hi.y);
+    v = __fadd_rn(v, hi.z);
+    v = __fadd_rn(v, hi.w);
+    xsum[i] = v;
   }
   __syncthreads();
-  for (int r = warp; r <= kExperts; r += kRtThreads / 32) {
-    if (r < kExperts) {
-      const uint8_t* wrow = L.rw + (size_t)r * kHidden;
-      float q[8][8];
-      float sc[8], bi[8];
+  if (warp < kRtWarps) {
+    const int rbase = blockIdx.y * kRtRows + warp * kRtRowsPerWarp;
+    const uint8_t* wrow = L.rw + (size_t)rbase * kHidden + lane * 8;
+    const int sw = (lane >> 2) & 1;
+    float acc[kRtRowsPerWarp][kRtTok];
 #pragma unroll
-      for (int blk = 0; blk < 8; blk++) {
-        const uint2 w = __ldg(reinterpret_cast<const uint2*>(wrow + blk * 256 + lane * 8));
+    for (int r = 0; r < kRtRowsPerWarp; r++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          q[blk][i] = byte_f(w.x, i);
-          q[blk][4 + i] = byte_f(w.y, i);
-        }
-        const int g = blk * 4 + (lane >> 3);
-        sc[blk] = ld16<BF16>(L.rs + r * 32, g);
-        bi[blk] = ld16<BF16>(L.rb + r * 32, g);
+      for (int t = 0; t < kRtTok; t++) acc[r][t] = 0.f;
+    uint2 wn[kRtRowsPerWarp];
+    uint16_t sn[kRtRowsPerWarp], bn[kRtRowsPerWarp];
+    auto fetch = [&](int blk) {
+      const int g = blk * 4 + (lane >> 3);
+#pragma unroll
+      for (int r = 0; r < kRtRowsPerWarp; r++) {
+        wn[r] = __ldg(reinterpret_cast<const uint2*>(wrow + (size_t)r * kHidden + blk * 256));
+        sn[r] = __ldg(L.rs + (size_t)(rbase + r) * (kHidden / kGroup) + g);
+        bn[r] = __ldg(L.rb + (size_t)(rbase + r) * (kHidden / kGroup) + g);
       }
-      for (int t = 0; t < tn; t++) {
-        float acc = 0.f;
+    };
+    fetch(0);
+#pragma unroll 1
+    for (int blk = 0; blk < 8; blk++) {
+      float q[kRtRowsPerWarp][8], sc[kRtRowsPerWarp], bi[kRtRowsPerWarp];
 #pragma unroll
-        for (int blk = 0; blk < 8; blk++) {
-          const float4* e4 = reinterpret_cast<const float4*>(xs + t * kHidden + blk * 256 + lane * 8);
-          const float4 a = e4[0], b = e4[1];
+      for (int r = 0; r < kRtRowsPerWarp; r++) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          q[r][k] = byte_f(wn[r].x, k);
+          q[r][4 + k] = byte_f(wn[r].y, k);
+        }
+        sc[r] = h16_to_f32<BF16>(sn[r]);
+        bi[r] = h16_to_f32<BF16>(bn[r]);
+      }
+      if (blk + 1 < 8) fetch(blk + 1);
+#pragma unroll
+      for (int t = 0; t < kRtTok; t++) {
+        const float4* e4 = reinterpret_cast<const float4*>(xs + t * kHidden + blk * 256 + lane * 8);
+        const float4 a = e4[sw], b = e4[sw ^ 1];
+        const float xsm = xsum[t * 256 + blk * 32 + lane];
+#pragma unroll
+        for (int r = 0; r < kRtRowsPerWarp; r++) {
           float dot = 0.f;
-          dot = __fmaf_rn(q[blk][0], a.x, dot);
-          dot = __fmaf_rn(q[blk][1], a.y, dot);
-          dot = __fmaf_rn(q[blk][2], a.z, dot);
-          dot = __fmaf_rn(q[blk][3], a.w, dot);
-          dot = __fmaf_rn(q[blk][4], b.x, dot);
-          dot = __fmaf_rn(q[blk][5], b.y, dot);
-          dot = __fmaf_rn(q[blk][6], b.z, dot);
-          dot = __fmaf_rn(q[blk][7], b.w, dot);
-          acc = __fmaf_rn(sc[blk], dot, acc);
-          acc = __fmaf_rn(bi[blk], xsum[t * 256 + blk * 32 + lane], acc);
+          dot = __fmaf_rn(q[r][0], a.x, dot);
+          dot = __fmaf_rn(q[r][1], a.y, dot);
+          dot = __fmaf_rn(q[r][2], a.z, dot);
+          dot = __fmaf_rn(q[r][3], a.w, dot);
+          dot = __fmaf_rn(q[r][4], b.x, dot);
+          dot = __fmaf_rn(q[r][5], b.y, dot);
+          dot = __fmaf_rn(q[r][6], b.z, dot);
+          dot = __fmaf_rn(q[r][7], b.w, dot);
+          acc[r][t] = __fmaf_rn(bi[r], xsm, __fmaf_rn(sc[r], dot, acc[r][t]));
         }
-        acc = warp_sum(acc);
-        if (lane == 0) logits[(size_t)(t0 + t) * kExperts + r] = acc;
       }
-    } else if (coef) {
-      const float cs = ld16<BF16>(L.cs, lane), cb = ld16<BF16>(L.cb, lane);
-      uint4 cw[4];
+    }
 #pragma unroll
-      for (int qq = 0; qq < 4; qq++) cw[qq] = __ldg(reinterpret_cast<const uint4*>(L.cw + lane * 64) + qq);
-      for (int t = 0; t < tn; t++) {
-        const float* e = xs + t * kHidden + lane * 64;
-        float acc = 0.f;
+    for (int r = 0; r < kRtRowsPerWarp; r++)
 #pragma unroll
-        for (int qq = 0; qq < 4; qq++)
-#pragma unroll
-          for (int d = 0; d < 4; d++)
-#pragma unroll
-            for (int k = 0; k < 4; k++)
-              acc = __fmaf_rn(__fmaf_rn(byte_f(word_of(cw[qq], d), k), cs, cb), e[qq * 16 + d * 4 + k], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) coef[t0 + t] = acc;
+      for (int t = 0; t < kRtTok; t++) {
+        const float v = warp_sum(acc[r][t]);
+        if (lane == ((r * kRtTok + t) & 31) && t < tn) logits[(size_t)(t0 + t) * kExperts + rbase + r] = v;
       }
+  } else if (coef && blockIdx.y == 0) {
+    const int t = lane;
+    if (t < tn) {
+      const float* xt = xs + t * kHidden;
+      float acc = 0.f;
+      for (int g = 0; g < kHidden / kGroup; g++) {
+        const float sc = ld16<BF16>(L.cs, g), bi = ld16<BF16>(L.cb, g);
+#pragma unroll 4
+        for (int u = 0; u < 16; u++) {
+          const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(L.cw + g * 64) + u);
+          const int c = g * 8 + (u >> 1);  // 8-element group
+          const float4 xv = *reinterpret_cast<const float4*>(xt + c * 8 + (((u & 1) ^ ((c >> 2) & 1)) << 2));
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 0), sc, bi), xv.x, acc);
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 1), sc, bi), xv.y, acc);
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 2), sc, bi), xv.z, acc);
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 3), sc, bi), xv.w, acc);
+        }
+      }
+      coef[t0 + t] = acc;
     }
   }
 }
@@ -719,6 +779,11 @@ cudaError_t prefill_init_attributes() {
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_router_prefill<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem);
   if (e != cudaSuccess) return e;
+  // three router CTAs per SM need the largest shared-memory carveout
+  e = cudaFuncSetAttribute(k_router_prefill<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_router_prefill<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_grouped<false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_grouped<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
@@ -730,7 +795,7 @@ cudaError_t prefill_init_attributes() {
 
 cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
                                   const uint16_t* x, float* logits, float* coef) {
-  const int grid = (T + kRtTok - 1) / kRtTok;
+  const dim3 grid((T + kRtTok - 1) / kRtTok, kExperts / kRtRows);
   if (bf16)
     k_router_prefill<true><<<grid, kRtThreads, kRtSmem, st>>>(L, T, x, logits, coef);
   else

@@ -40,6 +40,18 @@ def zipf_bias(seed=3, s=1.1, lam=1.0):
     return bias
 
 
+@pytest.mark.parametrize("T", [65, 300])
+def test_prefill_router_bitexact(ctx, layer, T):
+    """Prefill router kernel (one thread per router row, lane partials folded
+    in the butterfly order): logits and shared-gate coefficient bit-exact."""
+    from qfmoe import router_logits, synth_hidden
+    x = synth_hidden(13, 0, T)
+    logits, coef = router_logits(ctx, layer, x.cuda())
+    ref_l, ref_c = O.router(O.OracleLayer.synth(0, 5, experts=[]), x.numpy().view(np.uint16))
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), ref_l.view(np.uint32))
+    assert np.array_equal(coef.cpu().numpy().view(np.uint32), ref_c.view(np.uint32))
+
+
 @pytest.mark.parametrize("T", [65, 200, 1000])
 def test_prefill_parity(ctx, layer, olayer, T):
     from qfmoe import block_forward, synth_hidden

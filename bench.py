@@ -36,6 +36,25 @@ COEF_BYTES = 2048 + 2 * 32 * 2                      # 2,176
 RECORD = 1_769_472
 GATE_UP_BYTES = 2 * (524_288 + 2 * 32_768)          # per record: 1,179,648
 METRIC = "MoE-block tokens/s and achieved HBM GB/s (vs ~8 TB/s) at batch-1 decode and 4K prefill"
+PREFILL_T = 4096
+HIDDEN, INTER, TOPK = 2048, 512, 8
+
+
+def gemm_flops(T: int):
+    """(routed, shared) FLOPs of the gate/up + down expert GEMMs for T tokens."""
+    per_row = 2 * (2 * INTER * HIDDEN + HIDDEN * INTER)
+    return float(T * TOPK * per_row), float(T * per_row)
+
+
+def zipf_bias(seed: int = 3, s: float = 1.1):
+    """Harness logit bias: expert popularity ~ Zipf(s) over a seeded permutation of ids."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(256)
+    p = 1.0 / np.arange(1, 257) ** s
+    bias = np.empty(256, np.float32)
+    bias[order] = np.log(p / p.max()).astype(np.float32)
+    return bias
 
 
 def parse():
@@ -47,6 +66,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-extras", action="store_true", help="skip the T=8/32/64 lines")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the 4096-token prefill block")
+    ap.add_argument("--prefill-tokens", type=int, default=PREFILL_T)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     return ap.parse_args()
 
@@ -292,6 +313,42 @@ def main():
         del g
         return res
 
+    def measure_prefill(T: int, steps: int, warmup: int):
+        """One MoE block over T tokens with Zipf(1.1) routing."""
+        L = layers[0]
+        bias = torch.from_numpy(zipf_bias()).to(dev)
+        xs = [Q.synth_hidden(2000 + rank, i * T, T).to(dev) for i in range(4)]
+        out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        for i in range(warmup):
+            Q.block_forward(ctx, L, xs[i % 4], logit_bias=bias, out=out)
+        _, idx, _ = Q.block_forward(ctx, L, xs[0], logit_bias=bias, out=out, return_routing=True)
+        cnt = np.bincount(idx.cpu().numpy().reshape(-1), minlength=256)
+        barrier()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for i in range(steps):
+            Q.block_forward(ctx, L, xs[i % 4], logit_bias=bias, out=out)
+        ev1.record()
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / steps
+        barrier()
+        ms_max = max_over_ranks(ms)
+        kernels = {}
+        for name in ("router", "topk", "gate_up", "down", "combine"):
+            Q.profile_begin(ctx, name, 64)
+            for i in range(8):
+                Q.block_forward(ctx, L, xs[i % 4], logit_bias=bias, out=out)
+            tot, n = Q.profile_end(ctx)
+            kernels[name] = tot / max(n, 1)
+        ctx.check()
+        routed, shared = gemm_flops(T)
+        gemm_ms = kernels["gate_up"] + kernels["down"]
+        return {"T": T, "ms_per_block": ms_max, "tokens_per_s": world * T / (ms_max / 1e3),
+                "kernel_ms": kernels, "gemm_ms": gemm_ms,
+                "routed_gemm_flops": routed, "shared_gemm_flops": shared,
+                "rows_per_expert": {"max": int(cnt.max()), "min": int(cnt.min()), "mean": float(cnt.mean())}}
+
     head = measure(args.batch, args.steps, args.warmup, profile=True)
     e2e = measure(args.batch, max(args.steps // 2, 1), max(args.warmup, 3), profile=False,
                   e2e=True)
@@ -302,6 +359,8 @@ def main():
             extras[str(T)] = {"tokens_per_s": r["tokens_per_s"], "ms_per_step": r["ms_per_step"],
                               "step_gbs": r["step_gbs"],
                               "step_frac_of_hbm": r["step_gbs"] / hbm_peak}
+
+    pre = None if args.no_prefill else measure_prefill(args.prefill_tokens, 20, 3)
 
     if rank == 0:
         cpu = None
@@ -340,6 +399,22 @@ def main():
             "clocks": head["clocks"],
             "decode_batches": extras,
         }
+        if pre is not None:
+            _, tc_peak, tc_kind = peaks()
+            gemm_tf = (pre["routed_gemm_flops"] + pre["shared_gemm_flops"]) / (pre["gemm_ms"] / 1e3) / 1e12
+            routed_tf = pre["routed_gemm_flops"] / (pre["gemm_ms"] / 1e3) / 1e12
+            line["prefill_4k"] = {
+                "workload": f"one MoE block, {pre['T']} tokens, Zipf(1.1) expert popularity through the "
+                            "harness logit bias (BASELINE configs[2])",
+                "tokens_per_s": pre["tokens_per_s"], "ms_per_block": pre["ms_per_block"],
+                "kernel_ms": pre["kernel_ms"], "rows_per_expert": pre["rows_per_expert"],
+                "roofline": {"bound": "tensor", "kernel": "k_grouped (gate/up + down launches)",
+                             "achieved": gemm_tf, "peak": tc_peak, "unit": "TFLOP/s",
+                             "frac": gemm_tf / tc_peak, "peak_kind": tc_kind,
+                             "flops_per_block": pre["routed_gemm_flops"] + pre["shared_gemm_flops"],
+                             "routed_only_tflops": routed_tf, "routed_only_frac": routed_tf / tc_peak,
+                             "traffic": None},
+            }
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

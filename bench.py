@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-extras", action="store_true", help="skip the T=8/32/64 lines")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 4096-token prefill block")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="measure only the prefill block (profiling runs); value = its tokens/s")
     ap.add_argument("--prefill-tokens", type=int, default=PREFILL_T)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     return ap.parse_args()
@@ -348,6 +350,26 @@ def main():
                 "kernel_ms": kernels, "gemm_ms": gemm_ms,
                 "routed_gemm_flops": routed, "shared_gemm_flops": shared,
                 "rows_per_expert": {"max": int(cnt.max()), "min": int(cnt.min()), "mean": float(cnt.mean())}}
+
+    if args.prefill_only:
+        pre = measure_prefill(args.prefill_tokens, args.steps, max(args.warmup, 3))
+        if rank == 0:
+            _, tc_peak, tc_kind = peaks()
+            gemm_tf = (pre["routed_gemm_flops"] + pre["shared_gemm_flops"]) / (pre["gemm_ms"] / 1e3) / 1e12
+            print(json.dumps({
+                "metric": "MoE-block prefill tokens/s (BASELINE configs[2])", "value": pre["tokens_per_s"],
+                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": pre["ms_per_block"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16 operands, f32 accumulation",
+                "data": "synthetic (seeded weights; fp16 hidden N(0,1) RMS-normalised)",
+                "config": {"workload": f"one MoE block, {pre['T']} tokens, Zipf(1.1) routing"},
+                "kernel_ms": pre["kernel_ms"], "rows_per_expert": pre["rows_per_expert"],
+                "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": tc_peak, "unit": "TFLOP/s",
+                             "frac": gemm_tf / tc_peak, "peak_kind": tc_kind, "traffic": None}}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     head = measure(args.batch, args.steps, args.warmup, profile=True)
     e2e = measure(args.batch, max(args.steps // 2, 1), max(args.warmup, 3), profile=False,

@@ -57,6 +57,34 @@ def zipf_bias(seed: int = 3, s: float = 1.1):
     return bias
 
 
+def cache_trace(n_tokens: int, layers: int, seed: int = 1, s: float = 1.2, reuse: int = 5,
+                p_reuse: float = 0.7):
+    """Routing of the cached-decode stream: per layer, expert
+    popularity ~ Zipf(s) over a seeded permutation of ids; with probability p_reuse a
+    token re-uses `reuse` of the previous token's 8 experts at that layer.  Returns
+    idx [n_tokens, layers, 8] int32 and routing weights [n_tokens, layers, 8]."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    p = 1.0 / np.arange(1, 257) ** s
+    p /= p.sum()
+    perms = [rng.permutation(256) for _ in range(layers)]
+    idx = np.zeros((n_tokens, layers, 8), np.int32)
+    for t in range(n_tokens):
+        for l in range(layers):
+            chosen = []
+            if t > 0 and rng.random() < p_reuse:
+                chosen = [int(e) for e in rng.choice(idx[t - 1, l], reuse, replace=False)]
+            while len(chosen) < 8:
+                for r in rng.choice(256, 16, p=p):
+                    e = int(perms[l][r])
+                    if e not in chosen and len(chosen) < 8:
+                        chosen.append(e)
+            idx[t, l] = chosen
+    w = rng.random((n_tokens, layers, 8)).astype(np.float32) + 0.05
+    w /= w.sum(-1, keepdims=True)
+    return idx, w
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -71,6 +99,13 @@ def parse():
                     help="measure only the prefill block (profiling runs); value = its tokens/s")
     ap.add_argument("--prefill-tokens", type=int, default=PREFILL_T)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cache-stream", action="store_true",
+                    help="skip the cached-decode stream (BASELINE configs[4])")
+    ap.add_argument("--cache-only", action="store_true",
+                    help="only the cached-decode stream; prints its own line")
+    ap.add_argument("--cache-tokens", type=int, default=512)
+    ap.add_argument("--cache-slots", type=int, default=2183)
+    ap.add_argument("--cache-policy", choices=["lru", "slru"], default="lru")
     return ap.parse_args()
 
 
@@ -351,6 +386,113 @@ def main():
                 "routed_gemm_flops": routed, "shared_gemm_flops": shared,
                 "rows_per_expert": {"max": int(cnt.max()), "min": int(cnt.min()), "mean": float(cnt.mean())}}
 
+    def measure_cache_stream(n_tokens: int, slots: int, policy: str):
+        """n_tokens batch-1 decode tokens through all layers with
+        routed experts served from `slots` HBM slots, backed by every layer-expert
+        record in pinned host memory.  Timed from a cold cache, end to end through
+        qf_moe_stream_step (planning, host->HBM record copies, the block stack, and
+        each token's hidden-state upload and output read-back)."""
+        from qfmoe.cache import ExpertCache, HostTier, stream_step
+        idx, w = cache_trace(n_tokens, args.layers, seed=1)
+        host = torch.empty((args.layers * 256, RECORD), dtype=torch.uint8, pin_memory=True)
+        for l, L in enumerate(layers):
+            host[l * 256:(l + 1) * 256].copy_(L.bank)
+        torch.cuda.synchronize()
+        cache = ExpertCache(slots, layer_count=args.layers, policy=policy)
+        tier = HostTier(local, slots, host)
+        xs = torch.stack([Q.synth_hidden(3000 + rank, t, 1) for t in range(n_tokens)]).pin_memory()
+        outs = torch.empty((n_tokens, 1, 2048), dtype=torch.float32).pin_memory()
+        x_dev = torch.empty((1, 2048), dtype=torch.float16, device=dev)
+        out_dev = torch.empty((1, 2048), dtype=torch.float32, device=dev)
+        ws = ctx.workspace(1)
+        # warm-up on the first tokens, then restart from a cold cache
+        wi, ww = cache_trace(8, args.layers, seed=101)
+        for t in range(8):
+            x_dev.copy_(xs[t], non_blocking=True)
+            stream_step(ctx, cache, tier, plan, wi[t], ww[t], x_dev, None, out_dev, 1e-6, workspace=ws)
+        torch.cuda.synchronize()
+        cache.clear()
+        cache.reset_metrics()
+        t0 = tier.stats()
+        barrier()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for t in range(n_tokens):
+            x_dev.copy_(xs[t], non_blocking=True)
+            stream_step(ctx, cache, tier, plan, idx[t], w[t], x_dev, None, out_dev, 1e-6, workspace=ws)
+            outs[t].copy_(out_dev, non_blocking=True)
+        ev1.record()
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        ctx.check()
+        barrier()
+        ms_max = max_over_ranks(ms)
+        m = cache.metrics_snapshot()
+        t1 = tier.stats()
+        copied = t1["bytes"] - t0["bytes"]
+        res = {"tokens": n_tokens, "slots": slots, "policy": policy, "ms_total": ms_max,
+               "tokens_per_s": world * n_tokens / (ms_max / 1e3),
+               "ms_per_token": ms_max / n_tokens,
+               "hits": m["hits"], "misses": m["misses"], "evictions": m["evictions"],
+               "hit_rate": m["hits"] / max(m["hits"] + m["misses"], 1),
+               "misses_per_token": m["misses"] / n_tokens,
+               "h2d_record_bytes": copied, "h2d_gbs": copied / (ms / 1e3) / 1e9,
+               "gpu_launches": n_tokens}
+        if rank == 0:
+            # the planner's hits against the oracle's LRU restatement on the same trace
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle as O
+            if policy == "lru":
+                ref = O.OracleLRU(slots, args.layers)
+                for t in range(n_tokens):
+                    for l in range(args.layers):
+                        ref.acquire(l, idx[t, l])
+            else:
+                ref = O.OracleCache(slots, 0.25, args.layers)
+                for t in range(n_tokens):
+                    for l in range(args.layers):
+                        ref.acquire(l, idx[t, l])
+                ref.hits = ref.metrics()["hits"]
+            res["oracle_hits"] = int(ref.hits)
+            res["hits_match_oracle"] = int(ref.hits) == m["hits"]
+        tier.close()
+        cache.close()
+        del host
+        return res
+
+    def cache_line(c):
+        return {
+            "workload": f"{c['tokens']} batch-1 decode tokens through {args.layers} MoE blocks, "
+                        f"{c['slots']} HBM expert slots ({c['policy'].upper()}) backed by all "
+                        f"{args.layers * 256} layer-expert records in pinned host memory; "
+                        "per-layer Zipf(1.2) routing with temporal locality (5 of the previous "
+                        "token's 8 experts re-used with probability 0.7), seed 1 (BASELINE configs[4])",
+            "tokens_per_s": c["tokens_per_s"], "ms_per_token": c["ms_per_token"],
+            "hit_rate": c["hit_rate"], "hits": c["hits"], "misses": c["misses"],
+            "misses_per_token": c["misses_per_token"], "evictions": c["evictions"],
+            "h2d_gbs": c["h2d_gbs"], "h2d_record_bytes": c["h2d_record_bytes"],
+            "oracle_hits": c.get("oracle_hits"), "hits_match_oracle": c.get("hits_match_oracle"),
+            "timing": "cold cache; CUDA events around the whole stream, end to end through "
+                      "qf_moe_stream_step with per-token hidden upload and output read-back",
+        }
+
+    if args.cache_only:
+        c = measure_cache_stream(args.cache_tokens, args.cache_slots, args.cache_policy)
+        if rank == 0:
+            print(json.dumps({
+                "metric": "cached-decode MoE tokens/s (BASELINE configs[4])", "value": c["tokens_per_s"],
+                "unit": "tokens/s", "n_gpus": world, "steps": c["tokens"], "warmup": 8,
+                "ms_per_step": c["ms_per_token"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded weights, seed = layer index; fp16 hidden N(0,1) RMS-normalised)",
+                "config": {"workload": cache_line(c)["workload"]},
+                "cache_stream": cache_line(c), "gpu_launches": c["gpu_launches"]}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
     if args.prefill_only:
         pre = measure_prefill(args.prefill_tokens, args.steps, max(args.warmup, 3))
         if rank == 0:
@@ -383,6 +525,8 @@ def main():
                               "step_frac_of_hbm": r["step_gbs"] / hbm_peak}
 
     pre = None if args.no_prefill else measure_prefill(args.prefill_tokens, 20, 3)
+    cst = None if args.no_cache_stream else measure_cache_stream(args.cache_tokens, args.cache_slots,
+                                                                 args.cache_policy)
 
     if rank == 0:
         cpu = None
@@ -437,6 +581,8 @@ def main():
                              "routed_only_tflops": routed_tf, "routed_only_frac": routed_tf / tc_peak,
                              "traffic": None},
             }
+        if cst is not None:
+            line["cache_stream"] = cache_line(cst)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -190,6 +190,106 @@ qf_status qf_moe_block_forward_static(int32_t scale_dtype, const qf_moe_layer *l
                                       const uint16_t *x, const float *residual, float *out,
                                       int32_t *idx_out, float *w_out, void *stream);
 
+/* ---- expert-slot cache ----------------------------------------------- */
+/* Host-side slot planner.  Replaces Q4BoundedExpertCache's planning state
+ * (Storage/Q4BoundedExpertCache.swift:52-365): slots partitioned by layer
+ * (eight per layer plus the measured per-layer weights for 40 layers,
+ * :64-123), a segmented LRU per layer (probationary / protected, :222-297),
+ * and acquireSlotsParallel's plan-then-fetch contract (:330-365).
+ * QF_CACHE_LRU keeps one least-recently-used order per layer instead. */
+typedef enum qf_cache_policy { QF_CACHE_SLRU = 0, QF_CACHE_LRU = 1 } qf_cache_policy;
+
+/* QwenExpertCacheMetrics (Runtime/Telemetry/QwenRuntimeTelemetry.swift:58-69). */
+typedef struct qf_cache_metrics_t {
+    int64_t capacity;
+    int64_t occupancy;
+    int64_t probationary_occupancy;
+    int64_t protected_occupancy;
+    int64_t hits;
+    int64_t misses;
+    int64_t evictions;
+    int64_t fetched_bytes;
+    int64_t prefetch_requests;
+    int64_t useful_prefetch_hits;
+    int64_t wasted_prefetches;
+} qf_cache_metrics_t;
+
+typedef struct qf_cache qf_cache;
+
+/* capacity >= 1 slot; layer_count: the model's layers (one partition per
+ * layer when capacity >= 8 * layer_count, else one shared partition);
+ * probationary_ratio in [0, 1] (reference default 0.25). */
+qf_status qf_cache_create(int32_t capacity, int32_t layer_count, double probationary_ratio,
+                          int32_t policy, qf_cache **out);
+void qf_cache_destroy(qf_cache *c);
+/* acquireSlotsParallel for one layer's top-k: slots[n'] (n' = min(n, 8)) are
+ * the slots that hold (or will hold) experts[0..n'); miss_pos[*n_miss] lists the
+ * positions whose expert is being fetched; fetch_expert/fetch_slot[*n_fetch]
+ * (up to 8 each, optional) are the copies to issue, in order.  Host memory. */
+qf_status qf_cache_acquire(qf_cache *c, int32_t layer, const uint32_t *experts, int32_t n,
+                           uint32_t *slots, uint32_t *miss_pos, int32_t *n_miss,
+                           uint32_t *fetch_expert, uint32_t *fetch_slot, int32_t *n_fetch);
+/* prefetch (:367-400): candidates not resident go into free slots of the layer
+ * while any is free; fetch lists as for acquire (each up to n entries). */
+qf_status qf_cache_prefetch(qf_cache *c, int32_t layer, const uint32_t *candidates, int32_t n,
+                            uint32_t *fetch_expert, uint32_t *fetch_slot, int32_t *n_fetch);
+qf_status qf_cache_clear(qf_cache *c);
+qf_status qf_cache_reset_metrics(qf_cache *c);
+qf_status qf_cache_get_metrics(const qf_cache *c, qf_cache_metrics_t *out);
+qf_status qf_cache_info(const qf_cache *c, int32_t *layer_count,
+                        int32_t *probationary_capacity, int32_t *protected_capacity);
+/* first[layer_count], count[layer_count]: each partition's slot range. */
+qf_status qf_cache_layer_slots(const qf_cache *c, int32_t *first, int32_t *count);
+
+/* Slot budget: QwenActiveStreamingMemoryConfiguration.make
+ * (Runtime/Generation/QwenActiveStreamingMemoryConfiguration.swift:95-135).
+ * Slots that fit in budget_gib GiB after the dense layers, recurrent state,
+ * constants, scratch, reserve and the KV cache of context_length tokens;
+ * QF_ERR_OOM (slots still written) when fewer than 40 * 8 fit. */
+qf_status qf_cache_plan_slots(int32_t budget_gib, int64_t context_length, int64_t *slots,
+                              uint64_t *estimated_bytes, uint64_t *target_bytes);
+
+/* HBM slot arena + pinned-host tier.  Replaces the cache buffer
+ * (Q4BoundedExpertCache.swift:23) and its parallel pread of packed records
+ * (:330-365): the arena holds `slots` records of 1,769,472 bytes on `device`;
+ * host_records (pinned, or any host memory) holds n_host_records records
+ * `host_record_stride` bytes apart, indexed by layer * experts + expert or
+ * however the caller numbers them. */
+typedef struct qf_tier qf_tier;
+qf_status qf_tier_create(int32_t device, int32_t slots, const void *host_records,
+                         int64_t n_host_records, uint64_t host_record_stride, qf_tier **out);
+void qf_tier_destroy(qf_tier *t);
+/* The arena as a record bank for qf_moe_layer.expert_bank (stride 1,769,472). */
+qf_status qf_tier_arena(const qf_tier *t, void **bank, uint64_t *stride);
+/* Copies host record host_index[i] into arena slot slot[i] (one cudaMemcpyAsync
+ * per record on the tier's stream), then makes consumer_stream (NULL: legacy
+ * default stream) wait for the copies. */
+qf_status qf_tier_fetch(qf_tier *t, const int64_t *host_index, const uint32_t *slot, int32_t n,
+                        void *consumer_stream);
+qf_status qf_tier_stats(const qf_tier *t, int64_t *copies, int64_t *bytes);
+qf_status qf_tier_synchronize(qf_tier *t);
+
+/* One batch-1 decode step through n_layers MoE blocks whose routed experts
+ * stream through the cache: the active-streaming forwardToken MoE loop
+ * (QwenQ4ActiveExpertStreamingRunner.swift:958-1381 with
+ * Q4BoundedExpertCache.acquireSlotsParallel per layer).
+ *   - Routing is supplied on the host: host_idx [n_layers * 8] expert ids and
+ *     host_w [n_layers * 8] weights, layer-major.
+ *   - The cache plans each layer's slots (it must have one partition per
+ *     layer: layer_count == n_layers); misses are copied from host record
+ *     layer * 256 + expert into their slots on the tier's stream, after the
+ *     last earlier step that read an evicted slot, so copies for this step
+ *     overlap the previous step's kernel.
+ *   - The blocks then run as one persistent kernel on the handle's stream,
+ *     reading routed records through the slot map (layers[l].expert_bank,
+ *     record_stride and bank_records are replaced by the tier's arena).
+ *   - x, residual, out: device, as for qf_moe_stack_forward at T = 1.
+ *   - At most four steps are in flight; the fifth waits on the host. */
+qf_status qf_moe_stream_step(qf_moe *h, qf_cache *c, qf_tier *t, const qf_moe_layer *layers,
+                             int32_t n_layers, const int32_t *host_idx, const float *host_w,
+                             const uint16_t *x, const float *residual, float *out, float eps,
+                             void *workspace, size_t workspace_bytes);
+
 /* ---- kernel timing (bench harness) ----------------------------------- */
 /* Records CUDA events around every launch of one kernel of the block
  * (0 router, 1 top-k/grouping, 2 gate/up, 3 down, 4 combine) issued on this

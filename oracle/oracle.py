@@ -281,3 +281,81 @@ class OracleCache:
 def slru_replay(trace, capacity: int) -> int:
     t = np.ascontiguousarray(trace, np.uint16)
     return int(lib().qfo_slru_replay(_ptr(t), len(t), capacity))
+
+
+# ---------------------------------------------------------------- plain-LRU policy
+class OracleLRU:
+    """Per-layer least-recently-used slot cache: the "LRU eviction" policy of
+    the cached-decode benchmark configuration, restated with the partitioning
+    and tie rules of Q4BoundedExpertCache (Storage/Q4BoundedExpertCache.swift:
+    slot ranges :64-123, victim search :253-297 with the protected segment
+    never used): a miss takes the lowest empty slot of the layer, else the
+    unlocked slot with the oldest access tick (lowest slot on ties); slots
+    returned earlier in the same acquire are locked.  Pure Python, small cases."""
+
+    def __init__(self, capacity, layer_count=40):
+        ref = OracleCache(capacity, 0.25, layer_count)
+        caps = ref.layer_capacities()
+        self.ranges = []
+        start = 0
+        for c in caps:
+            self.ranges.append((start, start + c))
+            start += c
+        self.key = [None] * capacity
+        self.tick_of = [0] * capacity
+        self.where = {}
+        self.tick = 0
+        self.hits = self.misses = self.evictions = 0
+
+    def acquire(self, layer, experts):
+        lo, hi = self.ranges[min(max(layer, 0), len(self.ranges) - 1)]
+        self.tick += 1
+        locked = set()
+        slots, fetches = [], []
+        for e in list(experts)[:8]:
+            k = (layer, int(e))
+            s = self.where.get(k)
+            if s is not None:
+                self.hits += 1
+                self.tick_of[s] = self.tick
+            else:
+                self.misses += 1
+                free = [t for t in range(lo, hi) if self.key[t] is None and t not in locked]
+                if free:
+                    s = free[0]
+                else:
+                    cand = [(self.tick_of[t], t) for t in range(lo, hi) if t not in locked]
+                    s = min(cand)[1] if cand else 0
+                    del self.where[self.key[s]]
+                    self.evictions += 1
+                self.key[s] = k
+                self.where[k] = s
+                self.tick_of[s] = self.tick
+                fetches.append((int(e), s))
+            locked.add(s)
+            slots.append(s)
+        return slots, fetches
+
+
+# ---------------------------------------------------------------- slot budget
+GIB = 1_073_741_824
+
+
+def plan_slots(budget_gib: int, context_length: int):
+    """QwenActiveStreamingMemoryConfiguration.make
+    (Runtime/Generation/QwenActiveStreamingMemoryConfiguration.swift:95-135,
+    constants :56-93; DenseLayerArena.totalByteLength = 22,456,448 at
+    QwenQ4ActiveExpertStreamingRunner.swift:9).  Returns (slots, estimated,
+    target, ok) with ok False where the reference throws insufficientBudget."""
+    layers, full, linear = 40, 10, 30
+    dense = layers * 22_456_448
+    recurrent = linear * (8192 * 4 * 4 + 32 * 128 * 128 * 4)
+    constants = (2048 * 4 + layers * 2 * 2048 * 4
+                 + linear * (8192 * 4 * 4 + 32 * 4 + 32 * 4 + 128 * 4) + full * 2 * 256 * 4)
+    fixed = dense + recurrent + constants + 1_341_348 + 366_570_000
+    kv = full * 2 * 2 * 256 * 2 * context_length
+    scratch = 16 * 4 * context_length
+    non_cache = fixed + kv + scratch
+    target = budget_gib * GIB
+    slots = max(0, target - non_cache) // RECORD_BYTES
+    return slots, non_cache + slots * RECORD_BYTES, target, slots >= layers * 8

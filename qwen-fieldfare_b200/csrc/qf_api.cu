@@ -7,21 +7,13 @@
 #include <vector>
 
 #include "../../include/qf_moe.h"
+#include "qf_handle.h"
 #include "qf_internal.h"
 
 namespace qf {
 void prof_release(Prof* p);
 }
 using qf::prof_release;
-
-struct qf_moe {
-  int device;
-  qf_moe_dims dims;
-  cudaStream_t stream;
-  int* d_status;
-  std::string err;
-  qf::Prof prof;
-};
 
 namespace {
 
@@ -41,7 +33,9 @@ struct DeviceGuard {
   }
 };
 
-qf_status fail(qf_moe* h, qf_status s, const char* fmt, const char* a = "") {
+}  // namespace
+
+qf_status qf::fail(qf_moe* h, qf_status s, const char* fmt, const char* a) {
   if (h) {
     char buf[512];
     snprintf(buf, sizeof(buf), fmt, a);
@@ -50,16 +44,22 @@ qf_status fail(qf_moe* h, qf_status s, const char* fmt, const char* a = "") {
   return s;
 }
 
-qf_status cuda_fail(qf_moe* h, cudaError_t e, const char* where) {
+qf_status qf::cuda_fail(qf_moe* h, cudaError_t e, const char* where) {
   if (h) h->err = std::string(where) + ": " + cudaGetErrorString(e);
   return QF_ERR_CUDA;
 }
+
+namespace {
+using qf::cuda_fail;
+using qf::fail;
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 cudaStream_t stream_of(const qf_moe* h) { return h->stream; }
 
-qf_status layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
+}  // namespace
+
+qf_status qf::layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
   if (!l) return fail(h, QF_ERR_ARG, "layer descriptor is NULL");
   if (!l->router_w || !l->router_s || !l->router_b || !l->coef_w || !l->coef_s || !l->coef_b ||
       !l->shared_record || !l->expert_bank)
@@ -87,6 +87,9 @@ qf_status layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
   w->bank_records = l->bank_records;
   return QF_OK;
 }
+
+namespace {
+using qf::layer_to_w;
 
 qf_status routing_args(qf_moe* h, const qf_routing* r, qf::RoutingArgs* a) {
   a->bias = nullptr;

@@ -758,8 +758,8 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused(const __grid_constant__ 
     // ---------------- phase E: top-k + grouping
     if (A.r.idx_in) {
       if (tid < npos) {
-        m->idx[tid] = A.r.idx_in[tid];
-        m->w[tid] = A.r.w_in[tid];
+        m->idx[tid] = A.r.idx_in[(size_t)l * npos + tid];
+        m->w[tid] = A.r.w_in[(size_t)l * npos + tid];
       }
     } else if (warp < T) {
       topk_warp(A.logits, A.r.bias, warp, lane, m->idx, m->w);
@@ -770,7 +770,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused(const __grid_constant__ 
       if (A.w_out) A.w_out[(size_t)l * npos + tid] = m->w[tid];
     }
     if (tid < npos) {
-      int rec = A.r.rec_of_pos ? A.r.rec_of_pos[tid] : m->idx[tid];
+      int rec = A.r.rec_of_pos ? A.r.rec_of_pos[(size_t)l * npos + tid] : m->idx[tid];
       if (rec < 0 || (unsigned)rec >= L.bank_records) {
         set_status(A.status, kStatusDevice);
         rec = 0;

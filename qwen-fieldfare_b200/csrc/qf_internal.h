@@ -94,7 +94,9 @@ cudaError_t router_topk(cudaStream_t st, int T, const float* logits, const float
 constexpr int kFusedMaxTokens = 8;
 size_t fused_workspace_bytes(int T);
 cudaError_t fused_init_attributes();
-// layers: host array of n_layers descriptors (passed by value to the kernel)
+// layers: host array of n_layers descriptors (passed by value to the kernel).
+// Supplied routing (r.idx_in / w_in / rec_of_pos) holds n_layers * T * 8
+// entries, layer-major.
 cudaError_t fused_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16, int T,
                         const uint16_t* x, const float* residual, float* out, float eps,
                         const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,

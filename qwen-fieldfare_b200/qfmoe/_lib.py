@@ -43,6 +43,13 @@ class RoutingDesc(C.Structure):
                 ("record_of_pos", C.c_void_p)]
 
 
+class CacheMetrics(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in (
+        "capacity", "occupancy", "probationary_occupancy", "protected_occupancy", "hits",
+        "misses", "evictions", "fetched_bytes", "prefetch_requests", "useful_prefetch_hits",
+        "wasted_prefetches")]
+
+
 # (name, restype, argtypes) for every symbol include/qf_moe.h declares.
 _P = C.c_void_p
 _I = C.c_int32
@@ -65,6 +72,25 @@ SIGNATURES = {
                                   _P, _P, _P, C.c_size_t]),
     "qf_moe_block_forward_static": (_S, [C.c_int32, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
                                          _P, _P, _P]),
+    "qf_cache_create": (_S, [_I, _I, C.c_double, _I, C.POINTER(_P)]),
+    "qf_cache_destroy": (None, [_P]),
+    "qf_cache_acquire": (_S, [_P, _I, _P, _I, _P, _P, C.POINTER(_I), _P, _P, C.POINTER(_I)]),
+    "qf_cache_prefetch": (_S, [_P, _I, _P, _I, _P, _P, C.POINTER(_I)]),
+    "qf_cache_clear": (_S, [_P]),
+    "qf_cache_reset_metrics": (_S, [_P]),
+    "qf_cache_get_metrics": (_S, [_P, C.POINTER(CacheMetrics)]),
+    "qf_cache_info": (_S, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
+    "qf_cache_layer_slots": (_S, [_P, _P, _P]),
+    "qf_cache_plan_slots": (_S, [_I, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_uint64),
+                                 C.POINTER(C.c_uint64)]),
+    "qf_tier_create": (_S, [_I, _I, _P, C.c_int64, C.c_uint64, C.POINTER(_P)]),
+    "qf_tier_destroy": (None, [_P]),
+    "qf_tier_arena": (_S, [_P, C.POINTER(_P), C.POINTER(C.c_uint64)]),
+    "qf_tier_fetch": (_S, [_P, _P, _P, _I, _P]),
+    "qf_tier_stats": (_S, [_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "qf_tier_synchronize": (_S, [_P]),
+    "qf_moe_stream_step": (_S, [_P, _P, _P, C.POINTER(MoELayerDesc), _I, _P, _P, _P, _P, _P,
+                                C.c_float, _P, C.c_size_t]),
     "qf_moe_profile_begin": (_S, [_P, _I, _I]),
     "qf_moe_profile_end": (_S, [_P, C.POINTER(C.c_float), C.POINTER(_I)]),
     "qf_synth_records": (_S, [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _P,

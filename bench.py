@@ -37,6 +37,7 @@ RECORD = 1_769_472
 GATE_UP_BYTES = 2 * (524_288 + 2 * 32_768)          # per record: 1,179,648
 METRIC = "MoE-block tokens/s and achieved HBM GB/s (vs ~8 TB/s) at batch-1 decode and 4K prefill"
 PREFILL_T = 4096
+EP_T = 16384
 HIDDEN, INTER, TOPK = 2048, 512, 8
 
 
@@ -106,6 +107,11 @@ def parse():
     ap.add_argument("--cache-tokens", type=int, default=512)
     ap.add_argument("--cache-slots", type=int, default=2183)
     ap.add_argument("--cache-policy", choices=["lru", "slru"], default="lru")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="skip the expert-parallel block (BASELINE configs[3])")
+    ap.add_argument("--ep-only", action="store_true",
+                    help="only the expert-parallel block; prints its own line")
+    ap.add_argument("--ep-tokens", type=int, default=EP_T)
     return ap.parse_args()
 
 
@@ -461,6 +467,87 @@ def main():
         del host
         return res
 
+    def measure_ep(T_total: int, steps: int, warmup: int):
+        """one MoE block over T_total tokens split evenly over
+        the ranks, routed experts sharded 256/world per GPU, uniform-random top-8
+        (seeded), rows exchanged by the EP kernels over NVLink."""
+        T = T_total // world
+        ep = Q.ExpertParallel(ctx, rank, world, max_tokens=T)
+        local = ep.local_layer(0, 0)
+        rng = np.random.default_rng(5000 + rank)
+        idx = np.argsort(rng.random((T, 256)), axis=1)[:, :8].astype(np.int32)
+        w = rng.random((T, 8)).astype(np.float32) + 0.05
+        w /= w.sum(1, keepdims=True)
+        idx_d = torch.from_numpy(idx).to(dev)
+        w_d = torch.from_numpy(w).to(dev)
+        xs = [Q.synth_hidden(4000 + rank, i * T, T).to(dev) for i in range(2)]
+        out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        for i in range(warmup):
+            ep.forward(local, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
+        ctx.check()
+        barrier()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for i in range(steps):
+            ep.forward(local, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
+        ev1.record()
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / steps
+        barrier()
+        ms_max = max_over_ranks(ms)
+        kernels = {}
+        for name in ("router", "dispatch", "gate_up", "down", "combine"):
+            Q.profile_begin(ctx, name, 64)
+            for i in range(6):
+                ep.forward(local, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
+            tot, n = Q.profile_end(ctx)
+            kernels[name] = max_over_ranks(tot / max(n, 1))
+        ctx.check()
+        # routed rows this rank sends to other ranks (4 KB each) and receives
+        owner = idx // ep.experts_per_rank
+        sent_remote = int((owner != rank).sum())
+        ep.close()
+        routed, shared = gemm_flops(T_total)
+        return {"T_total": T_total, "T_rank": T, "ms_per_block": ms_max,
+                "tokens_per_s": T_total / (ms_max / 1e3), "kernel_ms": kernels,
+                "gemm_flops_per_rank": (routed + shared) / world,
+                "remote_rows_sent_rank0": sent_remote,
+                "dispatch_remote_bytes_rank0": sent_remote * 4096}
+
+    def ep_line(r):
+        _, tc_peak, tc_kind = peaks()
+        gemm_ms = r["kernel_ms"]["gate_up"] + r["kernel_ms"]["down"]
+        tf = r["gemm_flops_per_rank"] / (gemm_ms / 1e3) / 1e12
+        return {
+            "workload": f"one MoE block over {r['T_total']} tokens ({r['T_rank']} per GPU), routed experts "
+                        f"sharded {256 // world} per GPU, uniform-random top-8 (seeded); dispatch and "
+                        "combine by the EP kernels over NVLink peer memory (BASELINE configs[3])",
+            "n_gpus": world, "tokens_per_s": r["tokens_per_s"], "ms_per_block": r["ms_per_block"],
+            "kernel_ms_max_over_ranks": r["kernel_ms"],
+            "roofline": {"bound": "tensor", "kernel": "k_grouped (gate/up + down, per rank)", "achieved": tf,
+                         "peak": tc_peak, "unit": "TFLOP/s", "frac": tf / tc_peak, "peak_kind": tc_kind},
+            "dispatch_remote_bytes_rank0": r["dispatch_remote_bytes_rank0"],
+            "timing": "CUDA events on each rank, max over ranks",
+        }
+
+    if args.ep_only:
+        r = measure_ep(args.ep_tokens, args.steps, max(args.warmup, 3))
+        if rank == 0:
+            line = ep_line(r)
+            print(json.dumps({
+                "metric": "expert-parallel MoE-block tokens/s (BASELINE configs[3])",
+                "value": r["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": r["ms_per_block"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16 operands, f32 accumulation",
+                "data": "synthetic (seeded weights; fp16 hidden N(0,1) RMS-normalised)",
+                "config": {"workload": line["workload"]}, "ep": line,
+                "gpu_launches": args.steps * 12}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
     def cache_line(c):
         return {
             "workload": f"{c['tokens']} batch-1 decode tokens through {args.layers} MoE blocks, "
@@ -527,6 +614,7 @@ def main():
     pre = None if args.no_prefill else measure_prefill(args.prefill_tokens, 20, 3)
     cst = None if args.no_cache_stream else measure_cache_stream(args.cache_tokens, args.cache_slots,
                                                                  args.cache_policy)
+    epr = None if args.no_ep else measure_ep(args.ep_tokens, 20, 3)
 
     if rank == 0:
         cpu = None
@@ -583,6 +671,8 @@ def main():
             }
         if cst is not None:
             line["cache_stream"] = cache_line(cst)
+        if epr is not None:
+            line["ep_16k"] = ep_line(epr)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -290,9 +290,45 @@ qf_status qf_moe_stream_step(qf_moe *h, qf_cache *c, qf_tier *t, const qf_moe_la
                              const uint16_t *x, const float *residual, float *out, float eps,
                              void *workspace, size_t workspace_bytes);
 
+/* ---- expert parallelism over NVLink ----------------------------------- */
+/* No counterpart in the reference (single GPU).  The 256 routed experts are
+ * split across `world` GPUs of one node, one process per GPU: rank r owns
+ * experts [r * 256/world, (r+1) * 256/world) and each rank routes its own
+ * tokens.  Every rank exports one device region (CUDA IPC); dispatch stores
+ * routed token rows straight into the owners' regions over NVLink, the owners
+ * run the grouped expert GEMMs on their own memory, and each rank pulls its
+ * result rows back and combines them in router order (outputs bit-identical to
+ * the single-GPU block).  All waits are bounded (QF_ERR_TIMEOUT via
+ * qf_moe_check).  Setup, collective over the ranks:
+ *   qf_ep_create -> qf_ep_ipc_handle -> (exchange the world handles on the
+ *   host, rank order) -> qf_ep_connect.
+ * Every rank must then make the same sequence of qf_moe_block_forward_ep
+ * calls.  Before qf_ep_destroy, all ranks must have finished their last call
+ * (a host barrier after synchronising the stream). */
+#define QF_EP_HANDLE_BYTES 64
+typedef struct qf_ep qf_ep;
+/* world in {1, 2, 4, 8}; max_tokens: the most tokens any rank passes per call
+ * (the same on every rank; it sizes the receive rows). */
+qf_status qf_ep_create(qf_moe *h, int32_t rank, int32_t world, int32_t max_tokens, qf_ep **out);
+qf_status qf_ep_ipc_handle(const qf_ep *ep, void *handle);
+/* handles: world * QF_EP_HANDLE_BYTES bytes in rank order (this rank's entry is ignored). */
+qf_status qf_ep_connect(qf_ep *ep, const void *handles);
+void qf_ep_destroy(qf_ep *ep);
+qf_status qf_ep_info(const qf_ep *ep, int32_t *experts_per_rank, int64_t *receive_rows,
+                     uint64_t *region_bytes);
+/* One MoE block over this rank's T tokens (T <= max_tokens), on the handle's
+ * stream.  layer->expert_bank holds this rank's 256/world experts in order
+ * (record i = expert rank * 256/world + i); router, coefficient and shared
+ * expert are the full replicated weights.  routing: logit_bias, or a supplied
+ * top-k (topk_idx/topk_w, global expert ids); record_of_pos is not supported. */
+qf_status qf_moe_block_forward_ep(qf_ep *ep, const qf_moe_layer *layer, int32_t T,
+                                  const uint16_t *x, const float *residual, float *out,
+                                  const qf_routing *routing, int32_t *idx_out, float *w_out);
+
 /* ---- kernel timing (bench harness) ----------------------------------- */
 /* Records CUDA events around every launch of one kernel of the block
- * (0 router, 1 top-k/grouping, 2 gate/up, 3 down, 4 combine) issued on this
+ * (0 router, 1 top-k/grouping, 2 gate/up, 3 down, 4 combine, 5 the persistent
+ * decode kernel, 6 expert-parallel dispatch) issued on this
  * handle until qf_moe_profile_end, which synchronises and returns the summed
  * duration of the first min(launches, max_launches) recorded launches.
  * Launches captured into a CUDA graph report their most recent replay.

@@ -78,6 +78,9 @@ def _declare(L):
     L.qfo_cache_probationary_capacity.restype = _i
     L.qfo_slru_replay.argtypes = [_p, C.c_int64, _i]
     L.qfo_slru_replay.restype = C.c_int64
+    L.qfo_gate_up.argtypes = [_p, _i, _p, _p]
+    L.qfo_down.argtypes = [_p, _i, _p, _p]
+    L.qfo_combine.argtypes = [_p, _p, _p, C.c_float, _p, _p]
 
 
 def _ptr(a):
@@ -196,6 +199,29 @@ def topk(logits: np.ndarray, k: int = TOPK, bias=None):
     for t in range(logits.shape[0]):
         lib().qfo_topk(logits[t].ctypes.data, _ptr(b), n, k, idx[t].ctypes.data, w[t].ctypes.data)
     return idx, w
+
+
+def expert_ffn(record: np.ndarray, x16: np.ndarray, bf16: bool = False) -> np.ndarray:
+    """y = D . (SiLU(G x) * (U x)) of one expert record for one fp16 token row
+    (qfo_gate_up then qfo_down, reference order)."""
+    x = np.ascontiguousarray(x16, np.uint16).view(np.float16).astype(np.float32)
+    act = np.empty(INTER, np.float32)
+    y = np.empty(HIDDEN, np.float32)
+    rec = np.ascontiguousarray(record, np.uint8)
+    lib().qfo_gate_up(_ptr(rec), int(bf16), _ptr(x), _ptr(act))
+    lib().qfo_down(_ptr(rec), int(bf16), _ptr(act), _ptr(y))
+    return y
+
+
+def combine(y8: np.ndarray, w8: np.ndarray, sh_y: np.ndarray, coef: float, residual=None):
+    """One token's combine: (residual + sigmoid(coef) * sh_y) + sum_k w_k y_k in router order."""
+    y8 = np.ascontiguousarray(y8, np.float32)
+    w8 = np.ascontiguousarray(w8, np.float32)
+    sh = np.ascontiguousarray(sh_y, np.float32)
+    res = None if residual is None else np.ascontiguousarray(residual, np.float32)
+    out = np.empty(HIDDEN, np.float32)
+    lib().qfo_combine(_ptr(y8), _ptr(w8), _ptr(sh), float(coef), _ptr(res), _ptr(out))
+    return out
 
 
 def rmsnorm_to_f16(h: np.ndarray, eps: float = 1e-6) -> np.ndarray:

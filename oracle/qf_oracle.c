@@ -391,6 +391,21 @@ void qfo_down(const uint8_t *rec, int bf16, const float *act, float *y) {
 
 /* One token through the block, in the production streaming order
  * (QwenQ4ActiveExpertStreamingRunner.swift:1169-1381). */
+/* qwen_combine_cached_moe_subsets_f32 (deltanet.metal:2213-2227) with the
+ * shared down's gate (:2118-2120): out = (residual + sigmoid(c) * y_sh) +
+ * sum_k w_k y_k, the routed products summed in router order. */
+void qfo_combine(const float *y, const float *w, const float *sh_y, float c, const float *res,
+                 float *out) {
+    const float coeff = 1.0f / (1.0f + expf(-c));
+    for (int r = 0; r < QFO_HIDDEN; r++) {
+        const float shared = sh_y[r] * coeff;
+        float routed = y[r] * w[0];
+        for (int k = 1; k < QFO_TOPK; k++) routed = routed + y[(size_t)k * QFO_HIDDEN + r] * w[k];
+        const float base = res ? res[r] : 0.0f;
+        out[r] = (base + shared) + routed;
+    }
+}
+
 static void block_token(const qfo_layer *L, const uint16_t *x16, const float *res,
                         const float *bias, const int32_t *idx_in, const float *w_in, float *out,
                         int32_t *idx_out, float *w_out, float *logits_out, float *coef_out) {
@@ -414,7 +429,6 @@ static void block_token(const qfo_layer *L, const uint16_t *x16, const float *re
         if (logits_out) memcpy(logits_out, logits, sizeof(logits));
     }
     const float c = qfo_coef(L, x);
-    const float coeff = 1.0f / (1.0f + expf(-c));
     qfo_gate_up(L->shared_record, L->scale_bf16, x, sh_act);
     qfo_down(L->shared_record, L->scale_bf16, sh_act, sh_y);
     for (int k = 0; k < QFO_TOPK; k++) {
@@ -422,13 +436,7 @@ static void block_token(const qfo_layer *L, const uint16_t *x16, const float *re
         qfo_gate_up(rec, L->scale_bf16, x, act[k]);
         qfo_down(rec, L->scale_bf16, act[k], y[k]);
     }
-    for (int r = 0; r < QFO_HIDDEN; r++) {
-        const float shared = sh_y[r] * coeff;
-        float routed = y[0][r] * w[0];
-        for (int k = 1; k < QFO_TOPK; k++) routed = routed + y[k][r] * w[k];
-        const float base = res ? res[r] : 0.0f;
-        out[r] = (base + shared) + routed;
-    }
+    qfo_combine(&y[0][0], w, sh_y, c, res, out);
     if (idx_out) memcpy(idx_out, idx, sizeof(idx));
     if (w_out) memcpy(w_out, w, sizeof(w));
     if (coef_out) *coef_out = c;

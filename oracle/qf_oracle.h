@@ -105,6 +105,10 @@ void qfo_topk(const float *logits, const float *bias, int n, int k, int32_t *idx
 float qfo_coef(const qfo_layer *L, const float *x);
 void qfo_gate_up(const uint8_t *record, int scale_bf16, const float *x, float *act);
 void qfo_down(const uint8_t *record, int scale_bf16, const float *act, float *y);
+/* combine of one token: y [8][2048] in router order, w [8], shared y [2048],
+ * shared-gate pre-activation c, residual [2048] or NULL */
+void qfo_combine(const float *y, const float *w, const float *sh_y, float c, const float *res,
+                 float *out);
 
 /*
  * One MoE block over T tokens.

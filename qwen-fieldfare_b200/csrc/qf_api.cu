@@ -373,8 +373,8 @@ extern "C" {
 
 qf_status qf_moe_profile_begin(qf_moe* h, int32_t kernel_id, int32_t max_launches) {
   if (!h) return QF_ERR_ARG;
-  if (kernel_id < 0 || kernel_id > 5 || max_launches < 1 || max_launches > 65536)
-    return fail(h, QF_ERR_ARG, "kernel_id in [0,5], max_launches in [1,65536]");
+  if (kernel_id < 0 || kernel_id > 6 || max_launches < 1 || max_launches > 65536)
+    return fail(h, QF_ERR_ARG, "kernel_id in [0,6], max_launches in [1,65536]");
   DeviceGuard g(h->device);
   prof_release(&h->prof);
   h->prof.ev0 = new cudaEvent_t[max_launches];

@@ -38,6 +38,7 @@ constexpr int kMaxPositions = kDecodeMaxTokens * kTopK;  // 512
 // Device status word values (mirrors qf_status).
 constexpr int kStatusOk = 0;
 constexpr int kStatusDevice = -7;
+constexpr int kStatusTimeout = -6;
 
 struct LayerW {
   const uint8_t* rw;
@@ -83,6 +84,13 @@ __device__ __forceinline__ float byte_f(uint32_t w, int k) {
 // the vector's address (which would force it into local memory).
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int d) {
   return d == 0 ? v.x : (d == 1 ? v.y : (d == 2 ? v.z : v.w));
+}
+
+// fp16 (x0..x7) -> (x0,x4,x1,x5,x2,x6,x3,x7): the K order of the grouped GEMM
+// operands (the Q4 dequant then needs no byte permutes)
+__device__ __forceinline__ uint4 permute8(uint4 v) {
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                    __byte_perm(v.y, v.w, 0x7632));
 }
 
 __device__ __forceinline__ void set_status(int* status, int code) {

@@ -38,7 +38,6 @@ constexpr int kFMaxT = 8;
 constexpr int kFMaxPos = kFMaxT * kTopK;  // 64
 constexpr int kOutTiles = kHidden / 16;   // 128 output tiles of 16 rows
 constexpr unsigned kSpinLimit = 1u << 22;  // bounded waits: a few seconds at most
-constexpr int kStatusTimeout = -6;
 
 // ---- stage layouts (bytes) ----
 constexpr int kGuPitch = 1024 + 32;                  // padded gate/up row

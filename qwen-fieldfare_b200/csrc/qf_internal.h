@@ -47,7 +47,7 @@ struct Prof {
   cudaEvent_t* ev0 = nullptr;
   cudaEvent_t* ev1 = nullptr;
 };
-enum KernelId { kKRouter = 0, kKTopk = 1, kKGateUp = 2, kKDown = 3, kKCombine = 4, kKFused = 5 };
+enum KernelId { kKRouter = 0, kKTopk = 1, kKGateUp = 2, kKDown = 3, kKCombine = 4, kKFused = 5, kKDispatch = 6 };
 
 // Records the event pair of one launch of `kernel` when it is being profiled.
 struct ProfScope {
@@ -111,6 +111,18 @@ cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, i
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
                           float* w_out, void* workspace, int* status, Prof* prof);
+
+// grouped expert FFN over a row space (qf_prefill.cu): tiles of <= 128 rows per
+// expert from counts/offsets (expert 256 = the shared expert over T_shared rows
+// starting at *shared_base, or T_shared * 8), then gate/up -> act and down -> y.
+// rows: fp16 [R][2048] in the MMA K order; y row of routed row i = perm[i]
+// (perm NULL: i).
+size_t grouped_max_tiles(int T);
+cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, int T_shared,
+                      const int* shared_base, int4* tiles, int* n_tiles);
+cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
+                        __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
+                        size_t max_tiles, int sms, int* status, Prof* prof);
 
 // ---- dispatch plan (qf_route.cu)
 size_t dispatch_workspace_bytes(int T);

@@ -43,7 +43,6 @@ namespace qf {
 namespace {
 
 constexpr unsigned kSpin = 1u << 22;  // bounded waits (a few seconds at most)
-constexpr int kStatusTimeout = -6;
 
 __device__ __forceinline__ uint32_t s_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -152,11 +151,6 @@ __device__ __forceinline__ float h16_to_f32(uint16_t u) {
   }
 }
 
-// (x0..x7) -> (x0,x4,x1,x5,x2,x6,x3,x7): the K order of the GEMM operands
-__device__ __forceinline__ uint4 permute8(uint4 v) {
-  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
-                    __byte_perm(v.y, v.w, 0x7632));
-}
 
 // ------------------------------------------------------------------ router
 // Logits in the reference lane order (deltanet.metal:2229-2260): lane l of a
@@ -333,8 +327,10 @@ __global__ void __launch_bounds__(256) k_gather_rows(const int* __restrict__ per
 constexpr int kTileRows = 128;
 constexpr int kListThreads = 288;  // one thread per expert and the shared expert
 
+// shared_base (device, optional): first shared row; default T * 8.
 __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restrict__ counts,
                                                              const int* __restrict__ offsets, int T,
+                                                             const int* __restrict__ shared_base,
                                                              int4* __restrict__ tiles, int* __restrict__ n_tiles) {
   __shared__ int s_rem[kListThreads];
   __shared__ int s_warp[kListThreads / 32];
@@ -345,7 +341,7 @@ __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restric
     base = offsets[e];
   } else if (e == kExperts) {
     cnt = T;
-    base = T * kTopK;
+    base = shared_base ? *shared_base : T * kTopK;
   }
   const int full = cnt / kTileRows, rem = cnt % kTileRows;
   s_rem[e] = rem;
@@ -418,12 +414,11 @@ static_assert(kGemmSmem > 114 * 1024, "one CTA per SM: the kernel allocates all 
 struct GemmArgs {
   CUtensorMap map_rows;  // B operand rows: MODE 0 gathered x [P+T][2048], MODE 1 act [P+T][512]; box 64 x 128
   LayerW L;
-  const int* perm;
+  const int* perm;  // routed row -> y row (position t*8+k); NULL: the row itself
   const int4* tiles;
   const int* n_tiles;
   __half* act;  // MODE 0 output: [P+T][512] (permuted K)
   float* y;     // MODE 1 output: unweighted [P+T][2048]; routed row = position t*8+k
-  int P;        // routed positions (8T)
   int* status;
 };
 
@@ -587,7 +582,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       const int n = t.z;
       const int pb = t.w + t.y;  // first row of the tile in the row space
       if (MODE == 1) {
-        for (int c = et; c < n; c += kEpiThreads) sy->col_pos[i & 1][c] = shared ? pb + c : a.perm[pb + c];
+        for (int c = et; c < n; c += kEpiThreads)
+          sy->col_pos[i & 1][c] = (shared || !a.perm) ? pb + c : a.perm[pb + c];
         named_sync(2, kEpiThreads);
       }
       if (!mbar_wait(&sy->acc_full, i & 1)) ok = false;
@@ -803,6 +799,46 @@ cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, i
   return cudaGetLastError();
 }
 
+size_t grouped_max_tiles(int T) { return max_tiles_for(T); }
+
+cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, int T_shared,
+                      const int* shared_base, int4* tiles, int* n_tiles) {
+  k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T_shared, shared_base, tiles, n_tiles);
+  return cudaGetLastError();
+}
+
+cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
+                        __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
+                        size_t max_tiles, int sms, int* status, Prof* prof) {
+  GemmArgs g0, g1;
+  if (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows))
+    return cudaErrorInvalidValue;
+  g0.L = g1.L = L;
+  g0.perm = g1.perm = perm;
+  g0.tiles = g1.tiles = tiles;
+  g0.n_tiles = g1.n_tiles = n_tiles;
+  g0.act = g1.act = act;
+  g0.y = g1.y = y;
+  g0.status = g1.status = status;
+  const unsigned grid0 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<0>::PARTS);
+  {
+    ProfScope ps(prof, kKGateUp, st);
+    if (bf16)
+      k_grouped<true, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
+    else
+      k_grouped<false, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
+  }
+  const unsigned grid1 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<1>::PARTS);
+  {
+    ProfScope ps(prof, kKDown, st);
+    if (bf16)
+      k_grouped<true, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
+    else
+      k_grouped<false, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
                           float* w_out, void* workspace, int* status, Prof* prof) {
@@ -833,9 +869,6 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  GemmArgs g0, g1;
-  if (!encode_rows(&g0.map_rows, xs, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows))
-    return cudaErrorInvalidValue;
 
   {
     ProfScope ps(prof, kKRouter, st);
@@ -856,34 +889,11 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   if (e != cudaSuccess) return e;
   e = dispatch_plan_ws(st, idx, T, counts, offsets, perm, plan_ws, status);
   if (e != cudaSuccess) return e;
-  k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, tiles, n_tiles);
+  k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, nullptr, tiles, n_tiles);
   k_gather_rows<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(perm, (int)P, T, reinterpret_cast<const uint4*>(x),
                                                           reinterpret_cast<uint4*>(xs));
-
-  g0.L = g1.L = L;
-  g0.perm = g1.perm = perm;
-  g0.tiles = g1.tiles = tiles;
-  g0.n_tiles = g1.n_tiles = n_tiles;
-  g0.act = g1.act = act;
-  g0.y = g1.y = y;
-  g0.P = g1.P = (int)P;
-  g0.status = g1.status = status;
-  const unsigned grid0 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<0>::PARTS);
-  {
-    ProfScope ps(prof, kKGateUp, st);
-    if (bf16)
-      k_grouped<true, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
-    else
-      k_grouped<false, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
-  }
-  const unsigned grid1 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<1>::PARTS);
-  {
-    ProfScope ps(prof, kKDown, st);
-    if (bf16)
-      k_grouped<true, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
-    else
-      k_grouped<false, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
-  }
+  e = grouped_ffn(st, L, bf16, xs, R, act, y, perm, tiles, n_tiles, max_tiles, sms, status, prof);
+  if (e != cudaSuccess) return e;
   {
     ProfScope ps(prof, kKCombine, st);
     k_combine_weighted<<<T, 256, 0, st>>>(T, residual, y, w, y + P * kHidden, coef, out);

@@ -13,6 +13,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libqf_moe.so")
 
 QF_OK = 0
+EP_HANDLE_BYTES = 64
 STATUS_NAMES = {
     0: "QF_OK", -1: "QF_ERR_ARG", -2: "QF_ERR_CUDA", -3: "QF_ERR_NCCL", -4: "QF_ERR_OOM",
     -5: "QF_ERR_IO", -6: "QF_ERR_TIMEOUT", -7: "QF_ERR_DEVICE", -8: "QF_ERR_UNSUPPORTED",
@@ -91,6 +92,13 @@ SIGNATURES = {
     "qf_tier_synchronize": (_S, [_P]),
     "qf_moe_stream_step": (_S, [_P, _P, _P, C.POINTER(MoELayerDesc), _I, _P, _P, _P, _P, _P,
                                 C.c_float, _P, C.c_size_t]),
+    "qf_ep_create": (_S, [_P, _I, _I, _I, C.POINTER(_P)]),
+    "qf_ep_ipc_handle": (_S, [_P, _P]),
+    "qf_ep_connect": (_S, [_P, _P]),
+    "qf_ep_destroy": (None, [_P]),
+    "qf_ep_info": (_S, [_P, C.POINTER(_I), C.POINTER(C.c_int64), C.POINTER(C.c_uint64)]),
+    "qf_moe_block_forward_ep": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
+                                     C.POINTER(RoutingDesc), _P, _P]),
     "qf_moe_profile_begin": (_S, [_P, _I, _I]),
     "qf_moe_profile_end": (_S, [_P, C.POINTER(C.c_float), C.POINTER(_I)]),
     "qf_synth_records": (_S, [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _P,

@@ -108,9 +108,9 @@ class MoELayerWeights:
 
     @classmethod
     def synth(cls, ctx: MoEContext, seed: int, layer: int, n_records: int = EXPERTS,
-              bank: torch.Tensor | None = None):
-        """Seeded synthetic weights generated on the device (records 0..n_records-1
-        hold experts 0..n_records-1)."""
+              bank: torch.Tensor | None = None, expert0: int = 0):
+        """Seeded synthetic weights generated on the device (record i holds expert
+        expert0 + i; an expert-parallel rank passes its first expert)."""
         w = cls.allocate(ctx.device, 0 if bank is not None else n_records)
         if bank is not None:
             w.bank = bank
@@ -123,7 +123,8 @@ class MoELayerWeights:
         check(L.qf_synth_records(ctx.h, seed, layer, SHARED_EXPERT, 1, _ptr(w.shared),
                                  RECORD_BYTES), ctx.h)
         if w.bank.shape[0] > 0:
-            check(L.qf_synth_records(ctx.h, seed, layer, 0, min(w.bank.shape[0], EXPERTS),
+            check(L.qf_synth_records(ctx.h, seed, layer, expert0,
+                                     min(w.bank.shape[0], EXPERTS - expert0),
                                      _ptr(w.bank), w.bank.stride(0)), ctx.h)
         return w
 
@@ -243,7 +244,8 @@ def stack_forward(ctx: MoEContext, plan: StackPlan, x: torch.Tensor,
     return (out, idx, w) if return_routing else out
 
 
-KERNEL_IDS = {"router": 0, "topk": 1, "gate_up": 2, "down": 3, "combine": 4, "fused": 5}
+KERNEL_IDS = {"router": 0, "topk": 1, "gate_up": 2, "down": 3, "combine": 4, "fused": 5,
+              "dispatch": 6}
 
 
 def profile_begin(ctx: MoEContext, kernel: str, max_launches: int = 4096) -> None:

@@ -612,8 +612,9 @@ def main():
                               "step_frac_of_hbm": r["step_gbs"] / hbm_peak}
 
     pre = None if args.no_prefill else measure_prefill(args.prefill_tokens, 20, 3)
-    cst = None if args.no_cache_stream else measure_cache_stream(args.cache_tokens, args.cache_slots,
-                                                                 args.cache_policy)
+    # the cached stream is a single-GPU configuration (its host tier pins ~18 GB)
+    cst = None if (args.no_cache_stream or world > 1) else measure_cache_stream(
+        args.cache_tokens, args.cache_slots, args.cache_policy)
     epr = None if args.no_ep else measure_ep(args.ep_tokens, 20, 3)
 
     if rank == 0:

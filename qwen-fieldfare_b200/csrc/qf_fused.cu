@@ -510,7 +510,9 @@ __device__ void gu_task(const unsigned char* stage, const __half* xfrag, const f
 
 // top-k of token `t` by one warp: 8 rounds of (max value, then min index among
 // the lanes holding it) with warp reductions; orders ties like the reference's
-// strict-> insertion scan (deltanet.metal:2283-2329).
+// strict-> insertion scan (deltanet.metal:2283-2329).  Split in two halves so
+// that the weights (needed only by the combine) are computed off the critical
+// path.
 __device__ __forceinline__ uint32_t f2ord(float f) {
   const uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
@@ -518,14 +520,17 @@ __device__ __forceinline__ uint32_t f2ord(float f) {
 __device__ __forceinline__ float ord2f(uint32_t o) {
   return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
 }
-__device__ void topk_warp(const float* logits, const float* bias, int t, int lane, int* idx_out,
-                          float* w_out) {
+// Selection half: idx_out[t*8+k] and the selected (biased) logits sel_out[t*8+k];
+// the 256 biased logits go to vs[256] for the weights half.
+__device__ void topk_select(const float* logits, const float* bias, int t, int lane, int* idx_out,
+                            float* sel_out, float* vs) {
   float v[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int e = j * 32 + lane;
     const float lg = __ldcg(logits + t * kExperts + e);
     v[j] = bias ? __fadd_rn(lg, __ldg(bias + e)) : lg;
+    vs[e] = v[j];
   }
   unsigned taken = 0;
   float selv[kTopK];
@@ -549,6 +554,25 @@ __device__ void topk_warp(const float* logits, const float* bias, int t, int lan
     selv[k] = ord2f(mx);
     seli[k] = (int)win;
   }
+#pragma unroll
+  for (int k = 0; k < kTopK; k++)
+    if (lane == k) {
+      idx_out[t * kTopK + k] = seli[k];
+      sel_out[t * kTopK + k] = selv[k];
+    }
+}
+
+// Weights half: softmax over all 256 (biased) logits, renormalised over the
+// selected 8 (deltanet.metal:2283-2329); w[t*8+k] holds the selected logit on
+// entry and the weight on exit.
+__device__ void topk_weights(const float* vs, int t, int lane, float* w) {
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] = vs[j * 32 + lane];
+  float selv[kTopK];
+#pragma unroll
+  for (int k = 0; k < kTopK; k++) selv[k] = w[t * kTopK + k];
+  __syncwarp();
   const float mxv = selv[0];
   float den = 0.f;
 #pragma unroll
@@ -563,10 +587,7 @@ __device__ void topk_warp(const float* logits, const float* bias, int t, int lan
   }
 #pragma unroll
   for (int k = 0; k < kTopK; k++)
-    if (lane == k) {
-      idx_out[t * kTopK + k] = seli[k];
-      w_out[t * kTopK + k] = __fdiv_rn(p[k], ps);
-    }
+    if (lane == k) w[t * kTopK + k] = __fdiv_rn(p[k], ps);
 }
 
 // Task lists of the three phases by CTA-local index i.  R and E deal tasks
@@ -761,13 +782,10 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused(const __grid_constant__ 
         m->w[tid] = A.r.w_in[(size_t)l * npos + tid];
       }
     } else if (warp < T) {
-      topk_warp(A.logits, A.r.bias, warp, lane, m->idx, m->w);
+      // the weights are only needed by the combine: computed once the E stages are in flight
+      topk_select(A.logits, A.r.bias, warp, lane, m->idx, m->w, red + warp * kExperts);
     }
     __syncthreads();
-    if (blockIdx.x == 0 && tid < npos) {
-      if (A.idx_out) A.idx_out[(size_t)l * npos + tid] = m->idx[tid];
-      if (A.w_out) A.w_out[(size_t)l * npos + tid] = m->w[tid];
-    }
     if (tid < npos) {
       int rec = A.r.rec_of_pos ? A.r.rec_of_pos[(size_t)l * npos + tid] : m->idx[tid];
       if (rec < 0 || (unsigned)rec >= L.bank_records) {
@@ -810,6 +828,12 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused(const __grid_constant__ 
       const PhaseE dE{ng * 32};
       const int nE_my = n_mine(ng * 32 + 32);
       prime(L, nE_my, dE);
+      if (!A.r.idx_in && warp < T) topk_weights(red + warp * kExperts, warp, lane, m->w);
+      __syncthreads();
+      if (blockIdx.x == 0 && tid < npos) {
+        if (A.idx_out) A.idx_out[(size_t)l * npos + tid] = m->idx[tid];
+        if (A.w_out) A.w_out[(size_t)l * npos + tid] = m->w[tid];
+      }
       bool sh_staged = false;
       for (int i = 0; i < nE_my; i++) {
         const int task = dE.task(i);

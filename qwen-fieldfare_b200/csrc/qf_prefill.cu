@@ -87,6 +87,21 @@ __device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load3(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          s_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(s_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load4(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+          s_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(s_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void named_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
@@ -126,11 +141,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 32 bytes of Q4 codes straight into registers (read once; no L1 allocation)
-__device__ __forceinline__ void ld_codes32(const uint8_t* p, uint32_t (&r)[8]) {
-  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "l"(p));
-}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -384,15 +394,27 @@ __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restric
 //
 // Warp roles: 0-7 weight producers (warp w: block w >> 2, TMEM lanes
 // 32 * (w & 3) ...), 8-15 epilogue, 16-17 MMA issue (one thread each; warp 16
-// also allocates TMEM), 18 token loads (one thread issues the TMAs).
+// also allocates TMEM), 18 loads (one thread issues the TMAs).
+//
+// The weights reach shared memory by TMA too: per 64-column step one tiled
+// load brings the Q4 codes of the unit's 2 x 128 weight rows (32 bytes a row,
+// 8 KB) into a 6-stage ring, and per 8 steps one load each brings their
+// scales and biases (8 groups a row); producers read them from shared memory,
+// so the DRAM latency of the weights is covered by the ring, not by registers.
 constexpr int kGemmWarps = 19;
 constexpr int kGemmThreads = kGemmWarps * 32;
 constexpr int kMmaWarp = 16;
 constexpr int kLoadWarp = 18;
 constexpr int kEpiThreads = 256;
 constexpr int kTokStages = 8;
-constexpr int kAStages = 4;           // == the producers' register prefetch depth
+constexpr int kAStages = 4;           // TMEM A stages
 constexpr int kTokStageBytes = kTileRows * 128;  // 128 rows x 64 fp16, 128-byte swizzle
+constexpr int kCodeStages = 6;
+constexpr int kCodeStageBytes = 2 * 128 * 32;    // 2 blocks x 128 rows x 64 Q4 codes
+constexpr int kSbWin = 8;                        // steps per scale/bias window
+constexpr int kSbBufs = 2;
+constexpr int kSbHalf = 2 * 128 * kSbWin * 2;    // scales (or biases) of one window: 4 KB
+constexpr int kRingBytes = kTokStages * kTokStageBytes + kCodeStages * kCodeStageBytes + kSbBufs * 2 * kSbHalf;
 // TMEM columns: acc0 [0,128) | acc1 [128,256) | A stage s at 256 + 64 s (block 0 +0, block 1 +32)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = 256;
@@ -404,15 +426,22 @@ struct GemmSync {
   uint64_t a_empty[kAStages];
   uint64_t acc_full;
   uint64_t acc_empty;
+  uint64_t code_full[kCodeStages];
+  uint64_t code_empty[kCodeStages];
+  uint64_t sb_full[kSbBufs];
+  uint64_t sb_empty[kSbBufs];
   uint32_t tmem;
   int col_pos[2][kTileRows];        // down epilogue: output row of each column
 };
-constexpr int kGemmSmem = 1024 + kTokStages * kTokStageBytes + (int)sizeof(GemmSync);
+constexpr int kGemmSmem = 1024 + kRingBytes + (int)sizeof(GemmSync);
 static_assert(kGemmSmem <= 227 * 1024, "shared memory");
 static_assert(kGemmSmem > 114 * 1024, "one CTA per SM: the kernel allocates all of TMEM");
 
 struct GemmArgs {
   CUtensorMap map_rows;  // B operand rows: MODE 0 gathered x [P+T][2048], MODE 1 act [P+T][512]; box 64 x 128
+  // weights, [0] the bank, [1] the shared record: codes (box 32 bytes x 2 x 128
+  // rows), scales and biases (box 8 groups x 2 x 128 rows)
+  CUtensorMap map_code[2], map_s[2], map_b[2];
   LayerW L;
   const int* perm;  // routed row -> y row (position t*8+k); NULL: the row itself
   const int4* tiles;
@@ -452,39 +481,12 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 s2, __half2 b2,
   o[3] = *reinterpret_cast<uint32_t*>(&q3);
 }
 
-struct RowPtrs {
-  const uint8_t* w;
-  const uint16_t* s;
-  const uint16_t* b;
-};
-
 template <int MODE>
 struct Geo {
   static constexpr int K = MODE == 0 ? kHidden : kInter;
   static constexpr int KS = K / 64;
   static constexpr int PARTS = MODE == 0 ? kInter / 128 : kHidden / 256;
 };
-
-// the weight row a producer thread streams for unit u (block blk, TMEM lane r)
-template <int MODE>
-__device__ __forceinline__ RowPtrs unit_rows(const GemmArgs& a, int u, int blk, int r) {
-  const int4 t = a.tiles[u / Geo<MODE>::PARTS];
-  const int part = u % Geo<MODE>::PARTS;
-  const uint8_t* rec = t.x == kExperts ? a.L.shared : a.L.bank + (uint64_t)t.x * a.L.stride;
-  RowPtrs p;
-  if (MODE == 0) {
-    const int f = part * 128 + r;
-    p.w = rec + (blk ? kOffUpW : kOffGateW) + (size_t)f * (kHidden / 2);
-    p.s = reinterpret_cast<const uint16_t*>(rec + (blk ? kOffUpS : kOffGateS)) + f * (kHidden / kGroup);
-    p.b = reinterpret_cast<const uint16_t*>(rec + (blk ? kOffUpB : kOffGateB)) + f * (kHidden / kGroup);
-  } else {
-    const int f = part * 256 + blk * 128 + r;
-    p.w = rec + kOffDownW + (size_t)f * (kInter / 2);
-    p.s = reinterpret_cast<const uint16_t*>(rec + kOffDownS) + f * (kInter / kGroup);
-    p.b = reinterpret_cast<const uint16_t*>(rec + kOffDownB) + f * (kInter / kGroup);
-  }
-  return p;
-}
 
 __device__ __forceinline__ float silu_mul_fast(float g, float u) {
   const float e = __expf(fminf(-g, 80.0f));
@@ -499,7 +501,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* ring =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  GemmSync* sy = reinterpret_cast<GemmSync*>(ring + kTokStages * kTokStageBytes);
+  uint8_t* codes = ring + kTokStages * kTokStageBytes;
+  uint8_t* sbring = codes + kCodeStages * kCodeStageBytes;
+  GemmSync* sy = reinterpret_cast<GemmSync*>(ring + kRingBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = *a.n_tiles * PARTS;
@@ -518,6 +522,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
     }
     mbar_init(&sy->acc_full, 2);
     mbar_init(&sy->acc_empty, 8);
+    for (int s = 0; s < kCodeStages; s++) {
+      mbar_init(&sy->code_full[s], 1);
+      mbar_init(&sy->code_empty[s], 8);
+    }
+    for (int s = 0; s < kSbBufs; s++) {
+      mbar_init(&sy->sb_full[s], 1);
+      mbar_init(&sy->sb_empty[s], 8);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kMmaWarp) {
@@ -532,35 +544,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
   bool ok = true;
 
   if (warp < 8) {
-    // ---------------- weight producers: Q4 -> fp16 -> TMEM (A operand)
+    // ---------------- weight producers: Q4 (shared memory) -> fp16 -> TMEM (A operand)
     const int q = warp & 3, blk = warp >> 2, r = q * 32 + lane;
     const int total = my_units * KS;
-    uint32_t cw[kAStages][8];
-    uint32_t sb[kAStages];
-    int pu = 0, pks = 0;
-    RowPtrs pc = unit_rows<MODE>(a, blockIdx.x, blk, r);
-    auto fetch = [&](uint32_t(&dst)[8], uint32_t& dsb) {
-      ld_codes32(pc.w + pks * 32, dst);
-      dsb = (uint32_t)__ldg(pc.s + pks) | ((uint32_t)__ldg(pc.b + pks) << 16);
-      if (++pks == KS) {
-        pks = 0;
-        if (++pu < my_units) pc = unit_rows<MODE>(a, blockIdx.x + pu * G, blk, r);
-      }
-    };
-#pragma unroll
-    for (int j = 0; j < kAStages; j++) fetch(cw[j], sb[j]);
+    const int row_off = blk * 128 + r;
     const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + kTmemA + blk * 32;
     for (int g = 0; g < total; g += kAStages) {
 #pragma unroll
       for (int j = 0; j < kAStages; j++) {
         const int flat = g + j;
-        const uint32_t sbits = half_bits<BF16>(sb[j] & 0xFFFFu), bbits = half_bits<BF16>(sb[j] >> 16);
+        const int ks = flat % KS, win = flat / kSbWin;  // windows never straddle units (KS % 8 == 0)
+        const int cs = flat % kCodeStages, sbuf = win % kSbBufs;
+        if (ks % kSbWin == 0 && !mbar_wait(&sy->sb_full[sbuf], (win / kSbBufs) & 1)) ok = false;
+        if (!mbar_wait(&sy->code_full[cs], (flat / kCodeStages) & 1)) ok = false;
+        const uint4* cp = reinterpret_cast<const uint4*>(codes + cs * kCodeStageBytes + row_off * 32);
+        const uint4 c0 = cp[0], c1 = cp[1];
+        const uint16_t* sbp = reinterpret_cast<const uint16_t*>(sbring + sbuf * 2 * kSbHalf);
+        const uint16_t sv = sbp[row_off * kSbWin + ks % kSbWin];
+        const uint16_t bv = sbp[kSbHalf / 2 + row_off * kSbWin + ks % kSbWin];
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sy->code_empty[cs]);
+          if (ks % kSbWin == kSbWin - 1) mbar_arrive(&sy->sb_empty[sbuf]);
+        }
+        const uint32_t sbits = half_bits<BF16>(sv), bbits = half_bits<BF16>(bv);
         const __half2 s2 = __halves2half2(__ushort_as_half(sbits), __ushort_as_half(sbits));
         const __half2 b2 = __halves2half2(__ushort_as_half(bbits), __ushort_as_half(bbits));
+        const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
         uint32_t o[32];
 #pragma unroll
-        for (int wi = 0; wi < 8; wi++) dequant_word(cw[j][wi], s2, b2, o + 4 * wi);
-        if (flat + kAStages < total) fetch(cw[j], sb[j]);
+        for (int wi = 0; wi < 8; wi++) dequant_word(cw[wi], s2, b2, o + 4 * wi);
         if (!mbar_wait(&sy->a_empty[j], ((flat / kAStages) & 1) ^ 1)) ok = false;
         tc_fence_after();
         tmem_st32(tbase + j * 64, o);
@@ -653,13 +666,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       }
     }
   } else if (lane == 0) {
-    // ---------------- token rows by TMA: one 2-D tile (64 columns x 128 rows) per step
+    // ---------------- loads by TMA, per 64-column step: the unit's weight codes
+    // (and every 8 steps their scales and biases), then the token tile
     int gs = 0;
     for (int i = 0; i < my_units; i++) {
       const int u = blockIdx.x + i * G;
       const int4 t = a.tiles[u / PARTS];
       const int pb = t.w + t.y;
+      const int part = u % PARTS;
+      const int src = t.x == kExperts ? 1 : 0;
+      const int rec = src ? 0 : t.x;
       for (int ks = 0; ks < KS; ks++, gs++) {
+        const int cs = gs % kCodeStages, win = gs / kSbWin, sbuf = win % kSbBufs;
+        if (ks % kSbWin == 0) {
+          if (!mbar_wait(&sy->sb_empty[sbuf], ((win / kSbBufs) & 1) ^ 1)) ok = false;
+          uint8_t* sd = sbring + sbuf * 2 * kSbHalf;
+          mbar_expect_tx(&sy->sb_full[sbuf], 2 * kSbHalf);
+          if (MODE == 0) {
+            tma_load4(sd, &a.map_s[src], ks, part * 128, 0, rec, &sy->sb_full[sbuf]);
+            tma_load4(sd + kSbHalf, &a.map_b[src], ks, part * 128, 0, rec, &sy->sb_full[sbuf]);
+          } else {
+            tma_load3(sd, &a.map_s[src], ks, part * 256, rec, &sy->sb_full[sbuf]);
+            tma_load3(sd + kSbHalf, &a.map_b[src], ks, part * 256, rec, &sy->sb_full[sbuf]);
+          }
+        }
+        if (!mbar_wait(&sy->code_empty[cs], ((gs / kCodeStages) & 1) ^ 1)) ok = false;
+        mbar_expect_tx(&sy->code_full[cs], kCodeStageBytes);
+        if (MODE == 0)
+          tma_load4(codes + cs * kCodeStageBytes, &a.map_code[src], ks * 32, part * 128, 0, rec, &sy->code_full[cs]);
+        else
+          tma_load3(codes + cs * kCodeStageBytes, &a.map_code[src], ks * 32, part * 256, rec, &sy->code_full[cs]);
         const int ts = gs % kTokStages;
         if (!mbar_wait(&sy->tok_empty[ts], ((gs / kTokStages) & 1) ^ 1)) ok = false;
         mbar_expect_tx(&sy->tok_full[ts], kTokStageBytes);
@@ -768,6 +804,40 @@ static bool encode_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// n-D tiled map without swizzle (weight codes, scales, biases)
+static bool encode_nd(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+                      const cuuint64_t* strides, const cuuint32_t* box) {
+  PFN_cuTensorMapEncodeTiled fn = encode_fn();
+  if (!fn) return false;
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(m, dt, rank, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Weight maps of one source (the bank, or the shared record as a bank of 1).
+// gate/up: codes [record][matrix gate|up][512 rows][1024 bytes], scales and
+// biases [record][matrix][512 rows][32 groups]; down: codes [record][2048
+// rows][256 bytes], scales and biases [record][2048 rows][8 groups].
+static bool encode_weights(GemmArgs* g, int src, int mode, const uint8_t* rec0, uint64_t n_rec, uint64_t stride) {
+  if (mode == 0) {
+    const cuuint64_t dc[4] = {1024, 512, 2, n_rec}, sc[3] = {1024, 589824, stride};
+    const cuuint32_t bc[4] = {32, 128, 2, 1};
+    const cuuint64_t ds[4] = {32, 512, 2, n_rec}, ss[3] = {64, 589824, stride};
+    const cuuint32_t bs[4] = {8, 128, 2, 1};
+    return encode_nd(&g->map_code[src], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, rec0 + kOffGateW, dc, sc, bc) &&
+           encode_nd(&g->map_s[src], CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, rec0 + kOffGateS, ds, ss, bs) &&
+           encode_nd(&g->map_b[src], CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, rec0 + kOffGateB, ds, ss, bs);
+  }
+  const cuuint64_t dc[3] = {256, 2048, n_rec}, sc[2] = {256, stride};
+  const cuuint32_t bc[3] = {32, 256, 1};
+  const cuuint64_t ds[3] = {8, 2048, n_rec}, ss[2] = {16, stride};
+  const cuuint32_t bs[3] = {8, 256, 1};
+  return encode_nd(&g->map_code[src], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, rec0 + kOffDownW, dc, sc, bc) &&
+         encode_nd(&g->map_s[src], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, rec0 + kOffDownS, ds, ss, bs) &&
+         encode_nd(&g->map_b[src], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, rec0 + kOffDownB, ds, ss, bs);
+}
+
 cudaError_t prefill_init_attributes() {
   if (!encode_fn()) return cudaErrorNotSupported;
   cudaError_t e;
@@ -812,6 +882,11 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
                         size_t max_tiles, int sms, int* status, Prof* prof) {
   GemmArgs g0, g1;
   if (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows))
+    return cudaErrorInvalidValue;
+  if (!encode_weights(&g0, 0, 0, L.bank, L.bank_records, L.stride) ||
+      !encode_weights(&g0, 1, 0, L.shared, 1, L.stride) ||
+      !encode_weights(&g1, 0, 1, L.bank, L.bank_records, L.stride) ||
+      !encode_weights(&g1, 1, 1, L.shared, 1, L.stride))
     return cudaErrorInvalidValue;
   g0.L = g1.L = L;
   g0.perm = g1.perm = perm;

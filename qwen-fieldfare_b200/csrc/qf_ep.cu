@@ -14,12 +14,15 @@
 //             the source's (token, k) order, so the owner's grouped GEMM reads
 //             contiguous rows of its own memory;
 //   GEMMs     the owner runs the grouped tcgen05 gate/up and down GEMMs over
-//             its received rows plus its own tokens' shared-expert rows, writing
-//             fp32 result rows into its exported region, then signals every rank;
-//   combine   each rank pulls its tokens' eight result rows from the owners with
-//             plain peer loads and forms residual + c*shared + sum_k w_k y_k in
-//             router order -- the same arithmetic as the single-GPU block, so
-//             the outputs are bit-identical to it.
+//             its received rows plus its own tokens' shared-expert rows; the
+//             down GEMM's epilogue stores each fp32 result row straight into the
+//             sending rank's result area (at the row's send index, from the
+//             return address dispatch left beside it), so the transfer back
+//             overlaps the remaining tiles; then it signals every rank;
+//   combine   each rank reads its tokens' eight result rows from its own region
+//             and forms residual + c*shared + sum_k w_k y_k in router order --
+//             the same arithmetic as the single-GPU block, so the outputs are
+//             bit-identical to it.
 // Counters are monotonically increasing (never reset) and every wait is bounded
 // (globaltimer deadline); an expired wait sets QF_ERR_TIMEOUT in the status word
 // and the kernel returns.
@@ -96,7 +99,9 @@ struct EpArgs {
   const uint4* x;        // [T][256] this rank's fp16 token rows
   uint8_t* peer[kMaxRanks];  // exported region of each rank (this rank's own included)
   size_t x_off, y_off;   // receive rows / result rows inside a region
-  int* loc_of_pos;       // [P] (owner << 24) | row of each position's result row
+  size_t ret_off;        // int [rows_cap]: return address of each received row
+  int pmax;              // result rows [0, pmax) are send rows, [pmax, pmax + T) shared rows
+  int* loc_of_pos;       // [P] send row of each position (its result row here)
   int* counts_local;     // [256] received rows per local expert (zero past epr)
   int* offsets_local;    // [256] first received row of each local expert
   int* q_rows;           // received routed rows (the shared rows follow them)
@@ -188,14 +193,14 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
       src_t = pos >> 3;
       if (e < 0 || e >= kExperts) {  // a bad supplied expert id: skipped, reported
         if (lane == 0) {
-          a.loc_of_pos[pos] = a.rank << 24;
+          a.loc_of_pos[pos] = j;
           set_status(a.status, kStatusDevice);
         }
         continue;
       }
       d = e / a.epr;
       row = s_base[e] + (j - a.offsets[e]);
-      if (lane == 0) a.loc_of_pos[pos] = (row >= 0 && row < a.rows_cap) ? ((d << 24) | row) : (a.rank << 24);
+      if (lane == 0) a.loc_of_pos[pos] = j;
     } else {
       d = a.rank;
       src_t = j - a.P;
@@ -205,6 +210,9 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
       if (lane == 0) set_status(a.status, kStatusDevice);
       continue;
     }
+    // where the owner's down GEMM sends this row's result
+    if (lane == 0)
+      reinterpret_cast<int*>(a.peer[d] + a.ret_off)[row] = (a.rank << 24) | (j < a.P ? j : a.pmax + src_t);
     const uint4* s = a.x + static_cast<size_t>(src_t) * (kHidden / 8);
     uint4* dst = reinterpret_cast<uint4*>(a.peer[d] + a.x_off) + static_cast<size_t>(row) * (kHidden / 8);
     uint4 vv[kHidden / 8 / 32];
@@ -234,8 +242,8 @@ __global__ void k_ep_signal_done(EpArgs a) {
   }
 }
 
-// out = (residual + sigmoid(c) * shared) + sum_k w_k * y_k in router order; y_k
-// pulled from the owners' regions.
+// out = (residual + sigmoid(c) * shared) + sum_k w_k * y_k in router order; the
+// owners have stored y_k into this rank's result area at the send row.
 __global__ void __launch_bounds__(256) k_ep_combine(const __grid_constant__ EpArgs a, const float* __restrict__ residual,
                                                     const float* __restrict__ w, const float* __restrict__ coef,
                                                     float* __restrict__ out) {
@@ -254,17 +262,14 @@ __global__ void __launch_bounds__(256) k_ep_combine(const __grid_constant__ EpAr
 #pragma unroll
   for (int k = 0; k < kTopK; k++) {
     wk[k] = w[t * kTopK + k];
-    const int loc = a.loc_of_pos[t * kTopK + k];
-    int d = loc >> 24, row = loc & 0xFFFFFF;
-    if (d < 0 || d >= a.world || row >= a.rows_cap) {
+    int row = a.loc_of_pos[t * kTopK + k];
+    if (row < 0 || row >= a.pmax) {
       if (threadIdx.x == 0) set_status(a.status, kStatusDevice);
-      d = a.rank;
       row = 0;
     }
-    yk[k] = reinterpret_cast<const float4*>(a.peer[d] + a.y_off) + static_cast<size_t>(row) * (kHidden / 4);
+    yk[k] = reinterpret_cast<const float4*>(a.peer[a.rank] + a.y_off) + static_cast<size_t>(row) * (kHidden / 4);
   }
-  const int q = *a.q_rows;
-  const float4* s4 = reinterpret_cast<const float4*>(a.peer[a.rank] + a.y_off) + static_cast<size_t>(q + t) * (kHidden / 4);
+  const float4* s4 = reinterpret_cast<const float4*>(a.peer[a.rank] + a.y_off) + static_cast<size_t>(a.pmax + t) * (kHidden / 4);
   const float4* r4 = residual ? reinterpret_cast<const float4*>(residual + static_cast<size_t>(t) * kHidden) : nullptr;
   float4* o4 = reinterpret_cast<float4*>(out + static_cast<size_t>(t) * kHidden);
   for (int i = threadIdx.x; i < kHidden / 4; i += 256) {
@@ -297,7 +302,7 @@ size_t al256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 struct qf_ep {
   qf_moe* h = nullptr;
   int device = 0, rank = 0, world = 1, epr = 256, t_max = 0, sms = 0;
-  size_t rows_cap = 0, region_bytes = 0, x_off = 0, y_off = 0, max_tiles = 0;
+  size_t rows_cap = 0, region_bytes = 0, x_off = 0, y_off = 0, ret_off = 0, max_tiles = 0;
   uint8_t* region = nullptr;
   uint8_t* peer[qf::kMaxRanks] = {};
   bool opened[qf::kMaxRanks] = {};
@@ -362,7 +367,8 @@ qf_status qf_ep_create(qf_moe* h, int32_t rank, int32_t world, int32_t max_token
   ep->rows_cap = static_cast<size_t>(world) * P + max_tokens;
   ep->x_off = qf::kSigBytes;
   ep->y_off = ep->x_off + al256(ep->rows_cap * qf::kHidden * 2);
-  ep->region_bytes = ep->y_off + al256(ep->rows_cap * qf::kHidden * 4);
+  ep->ret_off = ep->y_off + al256(ep->rows_cap * qf::kHidden * 4);
+  ep->region_bytes = ep->ret_off + al256(ep->rows_cap * 4);
   ep->max_tiles = qf::grouped_max_tiles(max_tokens * world);
   size_t wsb = 0;
   wsb += al256(4 * (size_t)max_tokens * qf::kExperts) + al256(4 * (size_t)max_tokens);
@@ -512,6 +518,8 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   for (int d = 0; d < qf::kMaxRanks; d++) a.peer[d] = ep->peer[d];
   a.x_off = ep->x_off;
   a.y_off = ep->y_off;
+  a.ret_off = ep->ret_off;
+  a.pmax = ep->t_max * qf::kTopK;
   a.loc_of_pos = ep->loc_of_pos;
   a.counts_local = ep->counts_local;
   a.offsets_local = ep->offsets_local;
@@ -525,10 +533,16 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   }
   e = cudaGetLastError();
   if (e == cudaSuccess) e = qf::tile_list(st, ep->counts_local, ep->offsets_local, T, ep->q_rows, ep->tiles, ep->n_tiles);
+  qf::EpOut out_route{};
+  for (int d = 0; d < qf::kMaxRanks; d++) out_route.peer[d] = ep->peer[d];
+  out_route.n_peers = ep->world;
+  out_route.rows_cap = static_cast<int>(ep->rows_cap);
+  out_route.y_off = ep->y_off;
+  out_route.ret = reinterpret_cast<const int*>(ep->region + ep->ret_off);
   if (e == cudaSuccess)
     e = qf::grouped_ffn(st, L, bf16, reinterpret_cast<const uint16_t*>(ep->region + ep->x_off), ep->rows_cap,
                         ep->act, reinterpret_cast<float*>(ep->region + ep->y_off), nullptr, ep->tiles, ep->n_tiles,
-                        ep->max_tiles, ep->sms, h->d_status, &h->prof);
+                        ep->max_tiles, ep->sms, h->d_status, &h->prof, &out_route);
   if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: grouped experts");
   qf::k_ep_signal_done<<<1, 32, 0, st>>>(a);
   {

@@ -118,11 +118,20 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
 // rows: fp16 [R][2048] in the MMA K order; y row of routed row i = perm[i]
 // (perm NULL: i).
 size_t grouped_max_tiles(int T);
+// Expert-parallel output of the down GEMM: ret[row] = (rank << 24) | r sends
+// result row `row` to row r of rank's result area (peer[rank] + y_off).
+struct EpOut {
+  uint8_t* peer[8];
+  int n_peers;
+  int rows_cap;
+  size_t y_off;
+  const int* ret;
+};
 cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, int T_shared,
                       const int* shared_base, int4* tiles, int* n_tiles);
 cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
                         __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
-                        size_t max_tiles, int sms, int* status, Prof* prof);
+                        size_t max_tiles, int sms, int* status, Prof* prof, const EpOut* ep);
 
 // ---- dispatch plan (qf_route.cu)
 size_t dispatch_workspace_bytes(int T);

@@ -432,6 +432,7 @@ struct GemmSync {
   uint64_t sb_empty[kSbBufs];
   uint32_t tmem;
   int col_pos[2][kTileRows];        // down epilogue: output row of each column
+  float* col_row[2][kTileRows];     // expert-parallel down epilogue: destination row (NULL: skipped)
 };
 constexpr int kGemmSmem = 1024 + kRingBytes + (int)sizeof(GemmSync);
 static_assert(kGemmSmem <= 227 * 1024, "shared memory");
@@ -448,6 +449,7 @@ struct GemmArgs {
   const int* n_tiles;
   __half* act;  // MODE 0 output: [P+T][512] (permuted K)
   float* y;     // MODE 1 output: unweighted [P+T][2048]; routed row = position t*8+k
+  EpOut ep;     // MODE 1 with ep.ret: result rows go to the ranks named by ep.ret
   int* status;
 };
 
@@ -595,8 +597,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       const int n = t.z;
       const int pb = t.w + t.y;  // first row of the tile in the row space
       if (MODE == 1) {
-        for (int c = et; c < n; c += kEpiThreads)
-          sy->col_pos[i & 1][c] = (shared || !a.perm) ? pb + c : a.perm[pb + c];
+        for (int c = et; c < n; c += kEpiThreads) {
+          if (!a.ep.ret) {
+            sy->col_pos[i & 1][c] = (shared || !a.perm) ? pb + c : a.perm[pb + c];
+            continue;
+          }
+          float* dst;
+          {
+            // (rank << 24) | row: the row of that rank's result area, stored
+            // over NVLink while the following tiles run
+            const int code = a.ep.ret[pb + c];
+            const int dr = code >> 24, row = code & 0xFFFFFF;
+            if (dr < 0 || dr >= a.ep.n_peers || row >= a.ep.rows_cap) {
+              set_status(a.status, kStatusDevice);
+              dst = nullptr;
+            } else {
+              dst = reinterpret_cast<float*>(a.ep.peer[dr] + a.ep.y_off) + (size_t)row * kHidden;
+            }
+          }
+          sy->col_row[i & 1][c] = dst;
+        }
         named_sync(2, kEpiThreads);
       }
       if (!mbar_wait(&sy->acc_full, i & 1)) ok = false;
@@ -619,25 +639,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
         }
       } else {
         const int f = part * 256 + eq * 32 + lane;
-        float* base = a.y + f;
         for (int c0 = cbeg; c0 < cend; c0 += 32) {
           uint32_t v0[32], v1[32];
           tmem_ld32(tmem + lrow + c0, v0);
           tmem_ld32(tmem + lrow + 128 + c0, v1);
           tmem_ld_wait();
+          if (a.ep.ret) {
 #pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (c0 + j < cend) {
-              float* d = base + (size_t)sy->col_pos[i & 1][c0 + j] * kHidden;
-              d[0] = __uint_as_float(v0[j]);
-              d[128] = __uint_as_float(v1[j]);
-            }
+            for (int j = 0; j < 32; j++)
+              if (c0 + j < cend) {
+                float* d = sy->col_row[i & 1][c0 + j];
+                if (d) {
+                  d[f] = __uint_as_float(v0[j]);
+                  d[f + 128] = __uint_as_float(v1[j]);
+                }
+              }
+          } else {
+            float* base = a.y + f;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (c0 + j < cend) {
+                float* d = base + (size_t)sy->col_pos[i & 1][c0 + j] * kHidden;
+                d[0] = __uint_as_float(v0[j]);
+                d[128] = __uint_as_float(v1[j]);
+              }
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sy->acc_empty);
     }
+    // peer stores are visible system-wide before the kernel that signals them runs
+    if (MODE == 1 && a.ep.ret) __threadfence_system();
   } else if (warp < kLoadWarp) {
     // ---------------- MMA issue: warp 16 -> block 0 / acc0, warp 17 -> block 1 / acc1
     if (lane == 0) {
@@ -879,7 +913,7 @@ cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, in
 
 cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
                         __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
-                        size_t max_tiles, int sms, int* status, Prof* prof) {
+                        size_t max_tiles, int sms, int* status, Prof* prof, const EpOut* ep) {
   GemmArgs g0, g1;
   if (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows))
     return cudaErrorInvalidValue;
@@ -895,6 +929,8 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
   g0.act = g1.act = act;
   g0.y = g1.y = y;
   g0.status = g1.status = status;
+  g0.ep = EpOut{};
+  g1.ep = ep ? *ep : EpOut{};
   const unsigned grid0 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<0>::PARTS);
   {
     ProfScope ps(prof, kKGateUp, st);
@@ -967,7 +1003,7 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, nullptr, tiles, n_tiles);
   k_gather_rows<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(perm, (int)P, T, reinterpret_cast<const uint4*>(x),
                                                           reinterpret_cast<uint4*>(xs));
-  e = grouped_ffn(st, L, bf16, xs, R, act, y, perm, tiles, n_tiles, max_tiles, sms, status, prof);
+  e = grouped_ffn(st, L, bf16, xs, R, act, y, perm, tiles, n_tiles, max_tiles, sms, status, prof, nullptr);
   if (e != cudaSuccess) return e;
   {
     ProfScope ps(prof, kKCombine, st);

@@ -1,0 +1,737 @@
+// qf_fused1.cu -- persistent decode kernel for ONE token (T = 1) through a
+// stack of MoE blocks: one cooperative launch, one CTA per SM (>= 128 SMs).
+//
+// A batch-1 block reads ~16.5 MB of weights, 2.6 us at HBM speed; what costs
+// time is the dependency chain x -> router -> top-8 -> gate/up -> down ->
+// combine -> RMSNorm -> next x.  This kernel shortens the time spent waiting
+// on memory along that chain:
+//   - weights that do not depend on the token (router rows, the shared-gate
+//     row, the shared expert) are copied into shared memory one layer ahead,
+//     into one of two per-layer buffers (layer parity);
+//   - right after top-k every CTA issues ALL of its routed weight rows (its
+//     gate/up tiles and the down rows of its output tile), ~110 KB per SM as
+//     16-byte cp.async from all 512 threads (about 14 per thread), so the
+//     routed set of the layer (~14 MB) is in flight at once; the down rows
+//     land while gate/up computes;
+//   - the 8 positions of the token are 8 records, no grouping (a record named
+//     twice is fetched twice).
+// Rows land at a padded pitch so that the mma.sync fragment reads are free of
+// bank conflicts.
+//
+// Work of CTA b per layer:
+//   R  b < 64: shared-expert gate/up row pairs [8b, 8b+8); 64 <= b < 96: router
+//      rows [8(b-64), +8) in the reference lane order (deltanet.metal:2229-2281);
+//      b == 96: the shared-gate coefficient row (deltanet.metal:863-902).
+//   E  top-8 (every CTA, one warp; deltanet.metal:2283-2329) -> issue the routed
+//      copies -> routed gate/up tiles i = b and b + G (< 256): position i / 32,
+//      row pairs [16 (i % 32), +16) (deltanet.metal:2155-2179).
+//   D  b < 128: output rows [16b, 16b + 16) of the 8 routed and the shared down
+//      projections (deltanet.metal:2181-2211, 2099-2122), the router-order
+//      combine (deltanet.metal:2213-2227) and the RMS partial of those rows for
+//      the next block's RMSNorm (deltanet.metal:18-53).
+// No grid barriers: every vector that crosses CTAs (logits + coefficient, the
+// activations, the block output + RMS partials) is written as 8-byte words
+// {32-bit value, layer tag}, single-copy atomic, and the consumers poll the
+// words until every tag is the layer's (bounded).  Single buffers suffice:
+// every CTA contributes gate/up tiles to every layer, so a writer of layer
+// l + 1 has, through the chain of data it waited for, seen every CTA finish
+// reading layer l's copy of the same buffer.
+// Arithmetic: exact Q4 dequant on mma.sync with fp32 accumulation (see
+// qf_persist.cuh), fixed reduction orders, so results are bit-reproducible run
+// to run; router logits are bit-exact with the CPU oracle.
+#include <math.h>
+
+#include "qf_persist.cuh"
+
+namespace qf {
+
+namespace {
+
+using namespace pk;
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxLayers = 64;
+
+// ---- tile layouts in shared memory (bytes)
+constexpr int kGuPitch = 1024 + 32;  // padded Q4 row, K = 2048
+constexpr int kDnPitch = 256 + 32;   // padded Q4 row, K = 512
+// MMA tile of a gate/up projection: rows 0..7 gate rows r..r+7, rows 8..15 up
+// rows r..r+7; then s[16][32] and b[16][32] (16-bit) in the same row order.
+constexpr int kGuTileBytes = 16 * kGuPitch + 2048;  // 18944
+// Down tile: 16 rows of K = 512, then s[16][8], b[16][8].
+constexpr int kDnTileBytes = 16 * kDnPitch + 512;  // 5120
+constexpr int kRPart = kGuTileBytes;               // R task: >= 8 router rows + s/b (17408)
+constexpr int kDiBytes = kRPart + kDnTileBytes;    // token-independent part of a CTA
+static_assert(8 * 2048 + 2 * 512 <= kRPart, "R part");
+
+constexpr int kNShGu = 64;                       // shared gate/up MMA tiles (8 row pairs)
+constexpr int kNRouter = 32;                     // router tasks (8 rows)
+constexpr int kNR = kNShGu + kNRouter + 1;       // + the coefficient row: 97 CTAs
+constexpr int kNGu = kTopK * (kInter / 16);      // routed gate/up tiles of 16 row pairs: 256
+constexpr int kNOut = kHidden / 16;              // output tiles: 128 CTAs
+constexpr int kMaxGu = 2;                        // routed gate/up tiles per CTA (G >= 128)
+constexpr int kMinGrid = kNGu / kMaxGu;          // 128
+constexpr int kRoutedBytes = kMaxGu * 2 * kGuTileBytes + kTopK * kDnTileBytes;  // 116736
+constexpr int kDnCols = kTopK + 1;               // down columns: 8 routed + shared
+constexpr int kItemsD = kDnCols * 4;             // (column, K-quarter) items of phase D
+
+struct Misc1 {
+  int idx[kTopK];
+  float w[kTopK];
+  int rec[kTopK];
+  float vs[kExperts];
+  int cols[kDnCols][8];  // cols[e] = {e, -1, ...}: MMA column 0 <- fragment column e
+  float res[16];         // residual of this CTA's output rows (layers > 0)
+  float coef;            // shared-gate coefficient of the layer
+  float inv;
+  int fail;
+};
+
+constexpr int kOffDi = 0;
+constexpr int kOffRouted = kOffDi + 2 * kDiBytes;
+constexpr int kPollWords = kDnCols * kInter / 2;      // largest polled vector: act, 2304 words
+static_assert(kPollWords >= kHidden + kHidden / 16 && kPollWords >= kExperts + 1, "poll area");
+constexpr int kOffPoll = kOffRouted + kRoutedBytes;   // u32 [kPollWords]
+constexpr int kOffXh = kOffPoll + kPollWords * 4;
+constexpr int kOffXfrag = kOffXh + kHidden * 2;        // [32 groups][1 col][4][32 B]
+constexpr int kOffAfrag = kOffXfrag + 32 * 128;        // [8 groups][9 cols][4][32 B]
+constexpr int kOffXS = kOffAfrag + 8 * kDnCols * 128;
+constexpr int kOffXC = kOffXS + 32 * 4;
+constexpr int kOffAS = kOffXC + 32 * 4;
+constexpr int kOffAC = kOffAS + 8 * kDnCols * 4;
+constexpr int kOffRed = kOffAC + 8 * kDnCols * 4;
+constexpr int kRedFloats = kItemsD * 16 + 16;
+constexpr int kOffMisc = (kOffRed + kRedFloats * 4 + 127) & ~127;
+constexpr int kOffBar = (kOffMisc + (int)sizeof(Misc1) + 127) & ~127;
+constexpr int kNBars = 5;  // dib[2] (token-independent, by layer parity), rgu[2], rdn
+constexpr int kSmemBytes = kOffBar + kNBars * 8;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+static_assert(kOffXfrag % 16 == 0 && kOffAfrag % 16 == 0 && kOffRouted % 128 == 0, "alignment");
+static_assert(kGuTileBytes % 16 == 0 && kDnTileBytes % 16 == 0 && kDiBytes % 128 == 0, "alignment");
+
+struct Fused1Args {
+  int n_layers;      // layers in this launch
+  int first_layer;   // global index of layer 0 of this launch
+  int total_layers;  // layers of the whole stack
+  const uint16_t* x0;
+  const float* res0;
+  float* out;
+  float eps;
+  RoutingArgs r;
+  int* idx_out;
+  float* w_out;
+  // 8-byte words {value bits, tag = global layer index + 1}, cleared per call
+  uint64_t* ll_logits;  // [257]: router logits, then the shared-gate coefficient
+  uint64_t* ll_act;     // [9 * 256]: fp16 pairs; rows 0..7 routed positions, 8 the shared expert
+  uint64_t* ll_h;       // [2048 + 128]: block output, then the RMS partials of its row tiles
+  int* status;
+  LayerW layers[kMaxLayers];
+};
+
+template <bool BF16>
+__device__ __forceinline__ float cvt16(uint16_t u) {
+  if constexpr (BF16) {
+    return __uint_as_float(static_cast<uint32_t>(u) << 16);
+  } else {
+    return __half2float(__ushort_as_half(u));
+  }
+}
+
+// ---- copies: 16-byte cp.async spread over all threads of the CTA (a TMA bulk
+// copy per row would cost ~40 ns of issue each, and rows must land at a padded
+// pitch); completion: every thread arrives on the stage's mbarrier (count =
+// kThreads) once its copies so far have landed.
+//
+// Chunks [0, rows << lg) of a block of rows (2^lg chunks of 16 B per row),
+// dealt round-robin over the threads starting at thread t0; returns the next
+// segment's t0 so that consecutive segments stay balanced.
+__device__ __forceinline__ int copy_block(unsigned char* dst, int dst_pitch, const uint8_t* src,
+                                          int src_pitch, int rows, int lg, int t0) {
+  const int n = rows << lg;
+  for (int c = (static_cast<int>(threadIdx.x) - t0) & (kThreads - 1); c < n; c += kThreads) {
+    const int r = c >> lg, q = c & ((1 << lg) - 1);
+    cp_async16(dst + r * dst_pitch + q * 16, src + static_cast<size_t>(r) * src_pitch + q * 16);
+  }
+  return (t0 + n) & (kThreads - 1);
+}
+// MMA gate/up tile of record `rec`, row pairs [r, r + 8): 8 gate + 8 up rows, then
+// gate S, up S, gate B, up B (8 rows x 64 B each)
+__device__ __forceinline__ int copy_gu(unsigned char* tile, const uint8_t* rec, int r, int t0) {
+  t0 = copy_block(tile, kGuPitch, rec + kOffGateW + static_cast<size_t>(r) * 1024, 1024, 8, 6, t0);
+  t0 = copy_block(tile + 8 * kGuPitch, kGuPitch, rec + kOffUpW + static_cast<size_t>(r) * 1024, 1024, 8, 6, t0);
+  unsigned char* sb = tile + 16 * kGuPitch;
+  t0 = copy_block(sb, 0, rec + kOffGateS + r * 64, 0, 1, 5, t0);
+  t0 = copy_block(sb + 512, 0, rec + kOffUpS + r * 64, 0, 1, 5, t0);
+  t0 = copy_block(sb + 1024, 0, rec + kOffGateB + r * 64, 0, 1, 5, t0);
+  return copy_block(sb + 1536, 0, rec + kOffUpB + r * 64, 0, 1, 5, t0);
+}
+// down tile of output rows [16 j, 16 j + 16): 16 rows of 256 B, then S and B (256 B each)
+__device__ __forceinline__ int copy_dn(unsigned char* tile, const uint8_t* rec, int j, int t0) {
+  t0 = copy_block(tile, kDnPitch, rec + kOffDownW + static_cast<size_t>(j) * 4096, 256, 16, 4, t0);
+  t0 = copy_block(tile + 16 * kDnPitch, 0, rec + kOffDownS + j * 256, 0, 1, 4, t0);
+  return copy_block(tile + 16 * kDnPitch + 256, 0, rec + kOffDownB + j * 256, 0, 1, 4, t0);
+}
+
+// The token-independent rows CTA b needs for layer L (all threads): its R task
+// and the shared expert's down tile of its output rows; completion on `bar`.
+__device__ void issue_di(const LayerW& L, int b, unsigned char* buf, uint64_t* bar) {
+  int t0 = 0;
+  if (b < kNShGu) {
+    t0 = copy_gu(buf, L.shared, 8 * b, t0);
+  } else if (b < kNShGu + kNRouter) {
+    const int r0 = 8 * (b - kNShGu);
+    t0 = copy_block(buf, 2048, L.rw + static_cast<size_t>(r0) * 2048, 2048, 8, 7, t0);
+    t0 = copy_block(buf + 8 * 2048, 0, reinterpret_cast<const uint8_t*>(L.rs + r0 * 32), 0, 1, 5, t0);
+    t0 = copy_block(buf + 8 * 2048 + 512, 0, reinterpret_cast<const uint8_t*>(L.rb + r0 * 32), 0, 1, 5, t0);
+  } else if (b < kNR) {
+    t0 = copy_block(buf, 0, L.cw, 0, 1, 7, t0);
+    t0 = copy_block(buf + 2048, 0, reinterpret_cast<const uint8_t*>(L.cs), 0, 1, 2, t0);
+    t0 = copy_block(buf + 2048 + 64, 0, reinterpret_cast<const uint8_t*>(L.cb), 0, 1, 2, t0);
+  }
+  if (b < kNOut) copy_dn(buf + kRPart, L.shared, b, t0);
+  cp_async_arrive(bar);
+}
+
+// One router row (warp) from shared memory: lane slices of the reference order
+// (deltanet.metal:2229-2260), then the xor-butterfly simd_sum.
+template <bool BF16>
+__device__ __forceinline__ float router_row(const unsigned char* buf, int w, const __half* xh, int lane) {
+  const uint8_t* wrow = buf + w * 2048;
+  const uint16_t* srow = reinterpret_cast<const uint16_t*>(buf + 8 * 2048) + w * 32;
+  const uint16_t* brow = reinterpret_cast<const uint16_t*>(buf + 8 * 2048 + 512) + w * 32;
+  float acc = 0.f;
+#pragma unroll
+  for (int blk = 0; blk < 8; blk++) {
+    const uint2 wv = *reinterpret_cast<const uint2*>(wrow + blk * 256 + lane * 8);
+    const int gq = blk * 4 + (lane >> 3);
+    const float sc = cvt16<BF16>(srow[gq]), bi = cvt16<BF16>(brow[gq]);
+    const uint4 hv = *reinterpret_cast<const uint4*>(xh + blk * 256 + lane * 8);
+    const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&hv.x));
+    const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&hv.y));
+    const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&hv.z));
+    const float2 p3 = __half22float2(*reinterpret_cast<const __half2*>(&hv.w));
+    const float e[8] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y, p3.x, p3.y};
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) dot = __fmaf_rn(byte_f(wv.x, i), e[i], dot);
+#pragma unroll
+    for (int i = 0; i < 4; i++) dot = __fmaf_rn(byte_f(wv.y, i), e[4 + i], dot);
+    float sum = e[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) sum = __fadd_rn(sum, e[i]);
+    acc = __fmaf_rn(sc, dot, acc);
+    acc = __fmaf_rn(bi, sum, acc);
+  }
+  return warp_sum(acc);
+}
+
+// The shared-gate coefficient (one warp; deltanet.metal:863-902 with rows = 1):
+// lane l takes columns [64 l, 64 l + 64), dequantised element by element.
+template <bool BF16>
+__device__ __forceinline__ float coef_row(const unsigned char* buf, const __half* xh, int lane) {
+  const float cs = cvt16<BF16>(reinterpret_cast<const uint16_t*>(buf + 2048)[lane]);
+  const float cb = cvt16<BF16>(reinterpret_cast<const uint16_t*>(buf + 2048 + 64)[lane]);
+  uint4 cwv[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) cwv[q] = reinterpret_cast<const uint4*>(buf + lane * 64)[q];
+  float acc = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+#pragma unroll
+    for (int d = 0; d < 4; d++) {
+      const uint32_t wd = word_of(cwv[q], d);
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float xe = __half2float(xh[lane * 64 + q * 16 + d * 4 + k]);
+        acc = __fmaf_rn(__fmaf_rn(byte_f(wd, k), cs, cb), xe, acc);
+      }
+    }
+  }
+  return warp_sum(acc);
+}
+
+__device__ __forceinline__ uint32_t h2bits(__half lo, __half hi) {
+  return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+}
+
+// ---- 8-byte {value, tag} words
+__device__ __forceinline__ void ll_put(uint64_t* p, uint32_t v, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"((static_cast<uint64_t>(tag) << 32) | v)
+               : "memory");
+}
+__device__ __forceinline__ uint64_t ll_get(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// All threads: the values of words [0, n) once each carries `tag`, into dst
+// (dst[i] = value of word i).  Bounded: on expiry sets the status word and
+// *fail, and returns with dst partly stale.
+__device__ __forceinline__ void ll_poll(const uint64_t* src, int n, uint32_t tag, uint32_t* dst, int* status,
+                                        int* fail) {
+  constexpr int U = 5;
+  for (int base = 0; base < n; base += U * kThreads) {
+    uint64_t v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
+      if (i < n) v[u] = ll_get(src + i);
+    }
+    bool gave_up = false;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
+      if (i < n) {
+        unsigned spins = 0;
+        while (!gave_up && static_cast<uint32_t>(v[u] >> 32) != tag) {
+          if (++spins > kSpinLimit) {
+            set_status(status, kStatusTimeout);
+            *fail = 1;
+            gave_up = true;
+            break;
+          }
+          if (spins > 32) __nanosleep(64);
+          v[u] = ll_get(src + i);
+        }
+        dst[i] = static_cast<uint32_t>(v[u]);
+      }
+    }
+  }
+}
+// top-k selection of one token from logits in shared memory (one warp): the
+// order of pk::topk_select (ties to the lower index, deltanet.metal:2283-2329);
+// idx[k], the selected biased logits sel[k], and the 256 biased logits vs[].
+__device__ __forceinline__ void topk_select_smem(const float* logits, const float* bias, int lane, int* idx,
+                                                 float* sel, float* vs) {
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = j * 32 + lane;
+    v[j] = bias ? __fadd_rn(logits[e], __ldg(bias + e)) : logits[e];
+    vs[e] = v[j];
+  }
+  unsigned taken = 0;
+#pragma unroll
+  for (int k = 0; k < kTopK; k++) {
+    uint32_t best = 0;
+    int bj = 0;
+#pragma unroll
+    for (int j = 7; j >= 0; j--) {  // ties within a lane: lower j (lower expert id) wins
+      const uint32_t o = ((taken >> j) & 1u) ? 0u : f2ord(v[j]);
+      if (o >= best) {
+        best = o;
+        bj = j;
+      }
+    }
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t cand = (best == mx) ? static_cast<uint32_t>(bj * 32 + lane) : 0xffffffffu;
+    const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
+    if (static_cast<int>(win & 31) == lane) taken |= 1u << (win >> 5);
+    if (lane == k) {
+      idx[k] = static_cast<int>(win);
+      sel[k] = ord2f(mx);
+    }
+  }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ Fused1Args A) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  unsigned char* const routed = sm + kOffRouted;
+  uint32_t* const poll = reinterpret_cast<uint32_t*>(sm + kOffPoll);
+  __half* const xh = reinterpret_cast<__half*>(sm + kOffXh);
+  __half* const xfrag = reinterpret_cast<__half*>(sm + kOffXfrag);
+  __half* const afrag = reinterpret_cast<__half*>(sm + kOffAfrag);
+  float* const xS = reinterpret_cast<float*>(sm + kOffXS);
+  float* const xC = reinterpret_cast<float*>(sm + kOffXC);
+  float* const aS = reinterpret_cast<float*>(sm + kOffAS);
+  float* const aC = reinterpret_cast<float*>(sm + kOffAC);
+  float* const red = reinterpret_cast<float*>(sm + kOffRed);
+  Misc1* const m = reinterpret_cast<Misc1*>(sm + kOffMisc);
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + kOffBar);  // dib0, dib1, rgu0, rgu1, rdn
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.x, G = gridDim.x;
+  const bool has_r = b < kNR, has_d = b < kNOut, has_di = has_r || has_d;
+  const int n_gu = (b < kNGu ? 1 : 0) + (b + G < kNGu ? 1 : 0);
+  // Per mbarrier: phases completed so far (wait parity) and whether a phase is
+  // armed and not yet waited for.  Uniform across the CTA.
+  uint32_t phase[kNBars] = {0, 0, 0, 0, 0};
+  uint32_t armed = 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < kNBars; i++) mbar_init(&bars[i], kThreads);
+    m->fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (tid < kDnCols * 8) m->cols[tid >> 3][tid & 7] = (tid & 7) == 0 ? (tid >> 3) : -1;
+  __syncthreads();
+
+  // bounded wait for barrier i's armed phase (no-op when nothing is armed)
+  auto wait_bar = [&](int i) {
+    if (!((armed >> i) & 1u)) return;
+    if (!mbar_wait(&bars[i], phase[i] & 1u)) {
+      set_status(A.status, kStatusTimeout);
+      m->fail = 1;
+    }
+    phase[i]++;
+    armed &= ~(1u << i);
+  };
+  // leave after a failure: first wait (bounded) for this CTA's copies in flight
+  auto drain = [&]() {
+    for (int i = 0; i < kNBars; i++)
+      if ((armed >> i) & 1u) mbar_wait(&bars[i], phase[i] & 1u);
+  };
+
+  if (has_di) {
+    issue_di(A.layers[0], b, sm + kOffDi, &bars[0]);
+    armed |= 1u;
+    if (A.n_layers > 1) {
+      issue_di(A.layers[1], b, sm + kOffDi + kDiBytes, &bars[1]);
+      armed |= 2u;
+    }
+  }
+
+  for (int li = 0; li < A.n_layers; li++) {
+    const int l = A.first_layer + li;  // global layer index
+    const uint32_t tag = static_cast<uint32_t>(l) + 1u;
+    const int par = li & 1;
+    const LayerW& L = A.layers[li];
+    unsigned char* const di = sm + kOffDi + par * kDiBytes;
+    const bool last = (l == A.total_layers - 1);
+
+    // ---------------- prologue: x (fp16) and its MMA fragments
+    // x_0 is the input; x_l = fp16(h_l / rms(h_l)), the RMS summed over 128 row
+    // tiles of 16 rows (fma chain inside a tile, tiles summed in order).
+    if (l == 0) {
+      if (tid < kHidden / 8) reinterpret_cast<uint4*>(xh)[tid] = reinterpret_cast<const uint4*>(A.x0)[tid];
+    } else {
+      ll_poll(A.ll_h, kHidden + kNOut, tag - 1u, poll, A.status, &m->fail);
+      __syncthreads();
+      const float* hv = reinterpret_cast<const float*>(poll);
+      if (tid == 0) {
+        float tot = 0.f;
+        for (int c = 0; c < kNOut; c++) tot = __fadd_rn(tot, hv[kHidden + c]);
+        const float mean = __fdiv_rn(tot, (float)kHidden);
+        m->inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, A.eps)));
+      }
+      if (has_d && tid < 16) m->res[tid] = hv[16 * b + tid];
+      __syncthreads();
+      const float iv = m->inv;
+      const float4 h4 = reinterpret_cast<const float4*>(hv)[tid];
+      reinterpret_cast<__half2*>(xh)[2 * tid] =
+          __halves2half2(__float2half_rn(__fmul_rn(h4.x, iv)), __float2half_rn(__fmul_rn(h4.y, iv)));
+      reinterpret_cast<__half2*>(xh)[2 * tid + 1] =
+          __halves2half2(__float2half_rn(__fmul_rn(h4.z, iv)), __float2half_rn(__fmul_rn(h4.w, iv)));
+    }
+    __syncthreads();
+    stage_block<true, kThreads>(xh, 1, 32, kHidden, 1, xfrag, xS, xC);
+    __syncthreads();
+    if (m->fail) {
+      drain();
+      return;
+    }
+
+    // ---------------- phase R
+    if (has_r) {
+      wait_bar(par);
+      if (b < kNShGu) {
+        // shared gate/up row pairs [8b, 8b+8): warp w takes groups 2w, 2w+1
+        const uint16_t* s = reinterpret_cast<const uint16_t*>(di + 16 * kGuPitch);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_tile_smem<BF16, 2>(di, kGuPitch, 2 * warp, s, s + 512, 32, xfrag, xS, xC, 1, m->cols[0], acc,
+                               lane);
+        if ((lane & 3) == 0) {
+          red[warp * 16 + (lane >> 2)] = acc[0];
+          red[warp * 16 + 8 + (lane >> 2)] = acc[2];
+        }
+        __syncthreads();
+        if (tid < 8) {
+          float gs = 0.f, us = 0.f;
+#pragma unroll
+          for (int q = 0; q < kWarps; q++) {
+            gs = __fadd_rn(gs, red[q * 16 + tid]);
+            us = __fadd_rn(us, red[q * 16 + 8 + tid]);
+          }
+          const __half a = __float2half_rn(silu_mul(gs, us));
+          const __half a1 = __shfl_down_sync(0xffu, a, 1);
+          if ((tid & 1) == 0)
+            ll_put(A.ll_act + (kTopK * kInter + 8 * b + tid) / 2, h2bits(a, a1), tag);
+        }
+      } else if (b < kNShGu + kNRouter) {
+        if (warp < 8) {
+          const float v = router_row<BF16>(di, warp, xh, lane);
+          if (lane == 0) ll_put(A.ll_logits + 8 * (b - kNShGu) + warp, __float_as_uint(v), tag);
+        }
+      } else if (warp == 0) {
+        const float v = coef_row<BF16>(di, xh, lane);
+        if (lane == 0) ll_put(A.ll_logits + kExperts, __float_as_uint(v), tag);
+      }
+    }
+
+    // ---------------- phase E: top-k, routed copies, routed gate/up
+    ll_poll(A.ll_logits, kExperts + 1, tag, poll, A.status, &m->fail);
+    __syncthreads();
+    if (m->fail) {
+      drain();
+      return;
+    }
+    if (tid == 0) m->coef = __uint_as_float(poll[kExperts]);
+    if (A.r.idx_in) {
+      if (tid < kTopK) {
+        m->idx[tid] = A.r.idx_in[(size_t)l * kTopK + tid];
+        m->w[tid] = A.r.w_in[(size_t)l * kTopK + tid];
+      }
+    } else if (warp == 0) {
+      topk_select_smem(reinterpret_cast<const float*>(poll), A.r.bias, lane, m->idx, m->w, m->vs);
+    }
+    __syncthreads();
+    if (tid < kTopK) {
+      int rec = A.r.rec_of_pos ? A.r.rec_of_pos[(size_t)l * kTopK + tid] : m->idx[tid];
+      if (rec < 0 || (unsigned)rec >= L.bank_records) {
+        set_status(A.status, kStatusDevice);
+        rec = 0;
+      }
+      m->rec[tid] = rec;
+    }
+    __syncthreads();
+    {
+      // routed copies: gate/up tile u (two MMA tiles) on rgu[u], then the 8 down
+      // tiles of this CTA's output rows on rdn
+      int t0 = 0;
+      for (int u = 0; u < n_gu; u++) {
+        const int i = b + u * G, k = i >> 5, j = i & 31;
+        const uint8_t* rec = L.bank + static_cast<uint64_t>(m->rec[k]) * L.stride;
+        t0 = copy_gu(routed + (u * 2) * kGuTileBytes, rec, 16 * j, t0);
+        t0 = copy_gu(routed + (u * 2 + 1) * kGuTileBytes, rec, 16 * j + 8, t0);
+        cp_async_arrive(&bars[2 + u]);
+      }
+      if (has_d) {
+        for (int k = 0; k < kTopK; k++)
+          t0 = copy_dn(routed + kMaxGu * 2 * kGuTileBytes + k * kDnTileBytes,
+                       L.bank + static_cast<uint64_t>(m->rec[k]) * L.stride, b, t0);
+        cp_async_arrive(&bars[4]);
+      }
+    }
+    armed |= (n_gu > 0 ? 4u : 0u) | (n_gu > 1 ? 8u : 0u) | (has_d ? 16u : 0u);
+    // the weights are only needed by the combine: computed while the copies fly
+    if (!A.r.idx_in && warp == 1) topk_weights(m->vs, 0, lane, m->w);
+    for (int u = 0; u < n_gu; u++) {
+      wait_bar(2 + u);
+      const int i = b + u * G, k = i >> 5, j = i & 31;
+      // warp w: MMA tile w / 8 (row pairs +0 / +8), K-eighth w % 8 (4 groups)
+      const unsigned char* tb = routed + (u * 2 + (warp >> 3)) * kGuTileBytes;
+      const uint16_t* s = reinterpret_cast<const uint16_t*>(tb + 16 * kGuPitch);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_tile_smem<BF16, 4>(tb, kGuPitch, (warp & 7) * 4, s, s + 512, 32, xfrag, xS, xC, 1, m->cols[0],
+                             acc, lane);
+      if ((lane & 3) == 0) {
+        red[warp * 16 + (lane >> 2)] = acc[0];
+        red[warp * 16 + 8 + (lane >> 2)] = acc[2];
+      }
+      __syncthreads();
+      if (tid < 16) {
+        const int mt = tid >> 3, r = tid & 7;
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          gs = __fadd_rn(gs, red[(mt * 8 + q) * 16 + r]);
+          us = __fadd_rn(us, red[(mt * 8 + q) * 16 + 8 + r]);
+        }
+        const __half a = __float2half_rn(silu_mul(gs, us));
+        const __half a1 = __shfl_down_sync(0xffffu, a, 1);
+        if ((tid & 1) == 0)
+          ll_put(A.ll_act + (k * kInter + 16 * j + tid) / 2, h2bits(a, a1), tag);
+      }
+      __syncthreads();
+      if (m->fail) {
+        drain();
+        return;
+      }
+    }
+    if (b == 0 && tid < kTopK) {
+      if (A.idx_out) A.idx_out[(size_t)l * kTopK + tid] = m->idx[tid];
+      if (A.w_out) A.w_out[(size_t)l * kTopK + tid] = m->w[tid];
+    }
+
+    // ---------------- phase D: down projections, combine, RMS partials
+    if (has_d) {
+      float res_v = 0.f;
+      if (tid < 16) res_v = (l == 0) ? (A.res0 ? __ldg(A.res0 + 16 * b + tid) : 0.f) : m->res[tid];
+      ll_poll(A.ll_act, kPollWords, tag, poll, A.status, &m->fail);
+      __syncthreads();
+      stage_block<true, kThreads>(reinterpret_cast<const __half*>(poll), kDnCols, 8, kInter, kDnCols, afrag, aS,
+                                  aC);
+      wait_bar(par);
+      wait_bar(4);
+      __syncthreads();
+      if (m->fail) {
+        drain();
+        return;
+      }
+      for (int it = warp; it < kItemsD; it += kWarps) {
+        const int e = it >> 2, q = it & 3;  // column e (8 = shared), groups 2q, 2q+1
+        const unsigned char* tile =
+            e < kTopK ? routed + kMaxGu * 2 * kGuTileBytes + e * kDnTileBytes : di + kRPart;
+        const uint16_t* s = reinterpret_cast<const uint16_t*>(tile + 16 * kDnPitch);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_tile_smem<BF16, 2>(tile, kDnPitch, 2 * q, s, s + 128, 8, afrag, aS, aC, kDnCols, m->cols[e],
+                               acc, lane);
+        if ((lane & 3) == 0) {
+          red[it * 16 + (lane >> 2)] = acc[0];
+          red[it * 16 + 8 + (lane >> 2)] = acc[2];
+        }
+      }
+      __syncthreads();
+      if (tid < 16) {
+        const int r = 16 * b + tid;
+        float y[kDnCols];
+#pragma unroll
+        for (int e = 0; e < kDnCols; e++) {
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; q++) v = __fadd_rn(v, red[(e * 4 + q) * 16 + tid]);
+          y[e] = v;
+        }
+        const float coeff = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-m->coef)));
+        const float sh = __fmul_rn(y[kTopK], coeff);
+        float routed_sum = __fmul_rn(y[0], m->w[0]);
+#pragma unroll
+        for (int k = 1; k < kTopK; k++) routed_sum = __fadd_rn(routed_sum, __fmul_rn(y[k], m->w[k]));
+        const float v = __fadd_rn(__fadd_rn(res_v, sh), routed_sum);
+        // RMS partial of the 16 rows: fma chain in row order (lane 0 gathers)
+        float ssq = 0.f;
+#pragma unroll
+        for (int row = 0; row < 16; row++) {
+          const float vr = __shfl_sync(0xffffu, v, row);
+          ssq = __fmaf_rn(vr, vr, ssq);
+        }
+        if (last) {
+          A.out[r] = v;
+        } else {
+          ll_put(A.ll_h + r, __float_as_uint(v), tag);
+          if (tid == 0) ll_put(A.ll_h + kHidden + b, __float_as_uint(ssq), tag);
+        }
+      }
+    }
+    // every read of this layer's buffers is done: refill the parity buffer
+    // with layer li + 2's token-independent rows
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (m->fail) {
+      drain();
+      return;
+    }
+    if (has_di && li + 2 < A.n_layers) {
+      issue_di(A.layers[li + 2], b, di, &bars[par]);
+      armed |= 1u << par;
+    }
+  }
+}
+
+int g_fused1_grid[64] = {};  // per device: CTAs of the launch, -1 = unsupported
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+size_t fused1_workspace_bytes() {
+  auto a = [](size_t n) { return (n + 255) & ~(size_t)255; };
+  return a(8 * (kExperts + 1)) + a(8 * kPollWords) + a(8 * (kHidden + kNOut));
+}
+
+cudaError_t fused1_init_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(k_fused1<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_fused1<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+}
+
+cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16,
+                         const uint16_t* x, const float* residual, float* out, float eps,
+                         const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
+                         int* status, Prof* prof) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorNotSupported;
+  if (g_fused1_grid[dev] == 0) {
+    int sms = 0, per = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per, bf16 ? (const void*)k_fused1<true> : (const void*)k_fused1<false>, kThreads, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    // every CTA must own a routed gate/up tile (the ordering argument of the
+    // tagged words relies on it): at most 256 CTAs
+    const int grid = sms < kNGu ? sms : kNGu;
+    g_fused1_grid[dev] = (per >= 1 && grid >= kMinGrid) ? grid : -1;
+  }
+  if (g_fused1_grid[dev] < 0) return cudaErrorNotSupported;
+  // every bulk copy needs 16-byte aligned sources
+  if (!aligned16(x)) return cudaErrorNotSupported;
+  for (int i = 0; i < n_layers; i++) {
+    const LayerW& L = layers[i];
+    if (!aligned16(L.rw) || !aligned16(L.rs) || !aligned16(L.rb) || !aligned16(L.cw) || !aligned16(L.cs) ||
+        !aligned16(L.cb) || !aligned16(L.shared) || !aligned16(L.bank) || (L.stride & 15u) != 0)
+      return cudaErrorNotSupported;
+  }
+  char* p = static_cast<char*>(workspace);
+  auto take = [&](size_t n) {
+    char* q = p;
+    p += (n + 255) & ~(size_t)255;
+    return q;
+  };
+  Fused1Args A;  // layers by value: copied into the launch's parameter space
+  A.total_layers = n_layers;
+  A.x0 = x;
+  A.res0 = residual;
+  A.out = out;
+  A.eps = eps;
+  A.r = r;
+  A.idx_out = idx_out;
+  A.w_out = w_out;
+  A.ll_logits = reinterpret_cast<uint64_t*>(take(8 * (kExperts + 1)));
+  A.ll_act = reinterpret_cast<uint64_t*>(take(8 * kPollWords));
+  A.ll_h = reinterpret_cast<uint64_t*>(take(8 * (kHidden + kNOut)));
+  const size_t ll_bytes = static_cast<size_t>(p - reinterpret_cast<char*>(A.ll_logits));
+  // tags restart at 1 every call: clear the words of the previous call
+  e = cudaMemsetAsync(A.ll_logits, 0, ll_bytes, st);
+  if (e != cudaSuccess) return e;
+  A.status = status;
+  for (int l0 = 0; l0 < n_layers; l0 += kMaxLayers) {
+    const int n = n_layers - l0 < kMaxLayers ? n_layers - l0 : kMaxLayers;
+    A.first_layer = l0;
+    A.n_layers = n;
+    for (int i = 0; i < n; i++) A.layers[i] = layers[l0 + i];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g_fused1_grid[dev]);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // optional timing events around the launch (bench harness)
+    int slot = -1;
+    unsigned flags = cudaEventRecordDefault;
+    if (prof && prof->kernel == kKFused && prof->n < prof->cap) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cs);
+      if (cs == cudaStreamCaptureStatusActive) flags = cudaEventRecordExternal;
+      slot = prof->n++;
+      cudaEventRecordWithFlags(prof->ev0[slot], st, flags);
+    }
+    if (bf16)
+      e = cudaLaunchKernelEx(&cfg, k_fused1<true>, A);
+    else
+      e = cudaLaunchKernelEx(&cfg, k_fused1<false>, A);
+    if (slot >= 0) cudaEventRecordWithFlags(prof->ev1[slot], st, flags);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace qf

@@ -102,6 +102,16 @@ cudaError_t fused_stack(cudaStream_t st, const LayerW* layers, int n_layers, boo
                         const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
                         int* status, Prof* prof);
 
+// ---- persistent fused decode for one token (qf_fused1.cu); fused_stack calls
+// it for T == 1.  Returns cudaErrorNotSupported (having done nothing) when the
+// device has fewer than 128 SMs or a weight pointer is not 16-byte aligned.
+cudaError_t fused1_init_attributes();
+size_t fused1_workspace_bytes();
+cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16,
+                         const uint16_t* x, const float* residual, float* out, float eps,
+                         const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
+                         int* status, Prof* prof);
+
 // ---- prefill path, T > 64 (qf_prefill.cu)
 constexpr int kPrefillMaxTokens = 32768;
 size_t prefill_workspace_bytes(int T);

@@ -176,23 +176,25 @@ def test_block_logit_bias(ctx, layers, oracle_layers):
     assert max_rel(out.cpu().numpy(), ref["out"]) < TOL
 
 
-def test_block_bf16_scales():
+@pytest.mark.parametrize("T", [1, 2])
+def test_block_bf16_scales(T):
     from qfmoe import MoEContext, MoELayerWeights, block_forward
     c = MoEContext(0, scale_bf16=True)
     L = MoELayerWeights.synth(c, 9, 2)
     OL = O.OracleLayer.synth(9, 2, bf16=True)
-    x = hidden(2, tok0=50)
+    x = hidden(T, tok0=50)
     out, idx, _ = block_forward(c, L, x.cuda(), return_routing=True)
     ref = O.block(OL, x.numpy().view(np.uint16), threads=8)
     assert np.array_equal(idx.cpu().numpy(), ref["idx"])
     assert max_rel(out.cpu().numpy(), ref["out"]) < TOL
 
 
-@pytest.mark.parametrize("T", [3, 12])
+@pytest.mark.parametrize("T", [1, 3, 12])
 def test_stack_equals_chained_blocks_with_oracle_norm(ctx, layers, oracle_layers, T):
     """Two stacked blocks == block 0, the oracle's RMSNorm of its output, block 1:
     bitwise, which pins the in-kernel RMSNorm (deltanet.metal:18-53) to the oracle.
-    T = 3 runs the persistent kernel, T = 12 the per-kernel path."""
+    T = 1 runs the one-token persistent kernel, T = 3 the T <= 8 persistent
+    kernel, T = 12 the per-kernel path."""
     from qfmoe import StackPlan, block_forward, stack_forward
     x = hidden(T, tok0=40)
     plan = StackPlan([layers[(0, False)], layers[(1, False)]])
@@ -272,13 +274,14 @@ def test_persistent_and_per_kernel_paths_agree(ctx, layers, oracle_layers, T):
     assert max_rel(o2.cpu().numpy(), ref["out"]) < TOL
 
 
-def test_stack_long_chain_matches_blocks(ctx, layers):
-    """A 5-layer stack (layers 0,1,0,1,0) equals the chain of single blocks with the
-    in-kernel norm emulated by the oracle, bitwise."""
+@pytest.mark.parametrize("T,n_layers", [(2, 5), (1, 5), (1, 67)])
+def test_stack_long_chain_matches_blocks(ctx, layers, T, n_layers):
+    """A stack of alternating layers 0,1,0,... equals the chain of single blocks with
+    the in-kernel norm emulated by the oracle, bitwise.  67 layers at T = 1 cross
+    the 64-layer split of the persistent launch."""
     from qfmoe import StackPlan, block_forward, stack_forward
-    T = 2
     x = hidden(T, tok0=77)
-    seq = [layers[(0, False)], layers[(1, False)]] * 2 + [layers[(0, False)]]
+    seq = [layers[(l % 2, False)] for l in range(n_layers)]
     out = stack_forward(ctx, StackPlan(seq), x.cuda(), eps=1e-6)
     h = block_forward(ctx, seq[0], x.cuda())
     for L in seq[1:]:

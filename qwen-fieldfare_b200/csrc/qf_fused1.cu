@@ -90,8 +90,11 @@ struct Misc1 {
 
 constexpr int kOffDi = 0;
 constexpr int kOffRouted = kOffDi + 2 * kDiBytes;
-constexpr int kPollWords = kDnCols * kInter / 2;      // largest polled vector: act, 2304 words
-static_assert(kPollWords >= kHidden + kHidden / 16 && kPollWords >= kExperts + 1, "poll area");
+// The activations cross CTAs as fp16 pairs: 9 columns (8 routed positions,
+// then the shared expert) of 512 values.
+constexpr int kActWords = kDnCols * kInter / 2;  // 2304
+constexpr int kPollWords = kActWords;            // staging area (u32 words)
+static_assert(kPollWords >= kHidden + kHidden / 16 && kPollWords >= 2 * 8 * 4 * 32, "poll area");
 constexpr int kOffPoll = kOffRouted + kRoutedBytes;   // u32 [kPollWords]
 constexpr int kOffXh = kOffPoll + kPollWords * 4;
 constexpr int kOffXfrag = kOffXh + kHidden * 2;        // [32 groups][1 col][4][32 B]
@@ -193,37 +196,51 @@ __device__ void issue_di(const LayerW& L, int b, unsigned char* buf, uint64_t* b
   cp_async_arrive(bar);
 }
 
-// One router row (warp) from shared memory: lane slices of the reference order
-// (deltanet.metal:2229-2260), then the xor-butterfly simd_sum.
+// Router rows from shared memory in the reference lane order
+// (deltanet.metal:2229-2260): lane l of a row takes columns 8 l .. 8 l + 7 of
+// each 256-column block; per block a dot of the 8 codes with x (fma chain) and
+// the sum of the 8 x values (add chain), then acc = fma(s, dot, acc),
+// acc = fma(b, sum, acc) block after block, and finally the xor-butterfly
+// simd_sum.  Two warps share a row: one computes blocks 0..3, the other the
+// dots and sums of blocks 4..7, which the first folds into its chain.
 template <bool BF16>
-__device__ __forceinline__ float router_row(const unsigned char* buf, int w, const __half* xh, int lane) {
+__device__ __forceinline__ void router_blocks(const unsigned char* buf, int w, int h, const __half* xh, int lane,
+                                              float (&dot)[4], float (&sum)[4]) {
   const uint8_t* wrow = buf + w * 2048;
-  const uint16_t* srow = reinterpret_cast<const uint16_t*>(buf + 8 * 2048) + w * 32;
-  const uint16_t* brow = reinterpret_cast<const uint16_t*>(buf + 8 * 2048 + 512) + w * 32;
-  float acc = 0.f;
 #pragma unroll
-  for (int blk = 0; blk < 8; blk++) {
+  for (int i = 0; i < 4; i++) {
+    const int blk = 4 * h + i;
     const uint2 wv = *reinterpret_cast<const uint2*>(wrow + blk * 256 + lane * 8);
-    const int gq = blk * 4 + (lane >> 3);
-    const float sc = cvt16<BF16>(srow[gq]), bi = cvt16<BF16>(brow[gq]);
     const uint4 hv = *reinterpret_cast<const uint4*>(xh + blk * 256 + lane * 8);
     const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&hv.x));
     const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&hv.y));
     const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&hv.z));
     const float2 p3 = __half22float2(*reinterpret_cast<const __half2*>(&hv.w));
     const float e[8] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y, p3.x, p3.y};
-    float dot = 0.f;
+    float d = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; i++) dot = __fmaf_rn(byte_f(wv.x, i), e[i], dot);
+    for (int k = 0; k < 4; k++) d = __fmaf_rn(byte_f(wv.x, k), e[k], d);
 #pragma unroll
-    for (int i = 0; i < 4; i++) dot = __fmaf_rn(byte_f(wv.y, i), e[4 + i], dot);
-    float sum = e[0];
+    for (int k = 0; k < 4; k++) d = __fmaf_rn(byte_f(wv.y, k), e[4 + k], d);
+    float sm = e[0];
 #pragma unroll
-    for (int i = 1; i < 8; i++) sum = __fadd_rn(sum, e[i]);
-    acc = __fmaf_rn(sc, dot, acc);
-    acc = __fmaf_rn(bi, sum, acc);
+    for (int k = 1; k < 8; k++) sm = __fadd_rn(sm, e[k]);
+    dot[i] = d;
+    sum[i] = sm;
   }
-  return warp_sum(acc);
+}
+template <bool BF16>
+__device__ __forceinline__ float router_chain(const unsigned char* buf, int w, int h, int lane, const float (&dot)[4],
+                                              const float (&sum)[4], float acc) {
+  const uint16_t* srow = reinterpret_cast<const uint16_t*>(buf + 8 * 2048) + w * 32;
+  const uint16_t* brow = reinterpret_cast<const uint16_t*>(buf + 8 * 2048 + 512) + w * 32;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int gq = (4 * h + i) * 4 + (lane >> 3);
+    acc = __fmaf_rn(cvt16<BF16>(srow[gq]), dot[i], acc);
+    acc = __fmaf_rn(cvt16<BF16>(brow[gq]), sum[i], acc);
+  }
+  return acc;
 }
 
 // The shared-gate coefficient (one warp; deltanet.metal:863-902 with rows = 1):
@@ -265,69 +282,110 @@ __device__ __forceinline__ uint64_t ll_get(const uint64_t* p) {
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// All threads: the values of words [0, n) once each carries `tag`, into dst
-// (dst[i] = value of word i).  Bounded: on expiry sets the status word and
-// *fail, and returns with dst partly stale.
-__device__ __forceinline__ void ll_poll(const uint64_t* src, int n, uint32_t tag, uint32_t* dst, int* status,
-                                        int* fail) {
-  constexpr int U = 5;
-  for (int base = 0; base < n; base += U * kThreads) {
-    uint64_t v[U];
+// All threads: the values of words [0, n) once each carries `tag`, handed to
+// sink(i, value).  Each round re-issues every word that still
+// carries an older tag, so a round costs one memory round trip whatever the
+// count.  Bounded: on expiry sets the status word and *fail, and returns with
+// dst partly stale.
+template <int U>
+__device__ __forceinline__ bool ll_wait(const uint64_t* const (&src)[U], uint64_t (&v)[U], const bool (&use)[U],
+                                        uint32_t tag, int* status, int* fail) {
+  for (unsigned round = 0;; round++) {
+    bool ready = true;
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
-      if (i < n) v[u] = ll_get(src + i);
+    for (int u = 0; u < U; u++) ready &= !use[u] || static_cast<uint32_t>(v[u] >> 32) == tag;
+    if (ready) return true;
+    if (round > kSpinLimit) {
+      set_status(status, kStatusTimeout);
+      *fail = 1;
+      return false;
     }
-    bool gave_up = false;
+    if (round > 32) __nanosleep(64);
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      if (use[u] && static_cast<uint32_t>(v[u] >> 32) != tag) v[u] = ll_get(src[u]);
+  }
+}
+template <typename Sink>
+__device__ __forceinline__ void ll_poll(const uint64_t* src, int n, uint32_t tag, Sink sink, int* status,
+                                        int* fail) {
+  constexpr int U = 5;  // one pass covers the largest vector (2304 words)
+  for (int base = 0; base < n; base += U * kThreads) {
+    const uint64_t* p[U];
+    uint64_t v[U];
+    bool use[U];
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
-      if (i < n) {
-        unsigned spins = 0;
-        while (!gave_up && static_cast<uint32_t>(v[u] >> 32) != tag) {
-          if (++spins > kSpinLimit) {
-            set_status(status, kStatusTimeout);
-            *fail = 1;
-            gave_up = true;
-            break;
-          }
-          if (spins > 32) __nanosleep(64);
-          v[u] = ll_get(src + i);
-        }
-        dst[i] = static_cast<uint32_t>(v[u]);
-      }
+      use[u] = i < n;
+      p[u] = src + (use[u] ? i : 0);
+      v[u] = use[u] ? ll_get(p[u]) : 0;
+    }
+    ll_wait<U>(p, v, use, tag, status, fail);
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
+      if (use[u]) sink(i, static_cast<uint32_t>(v[u]));
     }
   }
 }
-// top-k selection of one token from logits in shared memory (one warp): the
-// order of pk::topk_select (ties to the lower index, deltanet.metal:2283-2329);
-// idx[k], the selected biased logits sel[k], and the 256 biased logits vs[].
-__device__ __forceinline__ void topk_select_smem(const float* logits, const float* bias, int lane, int* idx,
-                                                 float* sel, float* vs) {
-  float v[8];
+// Warp 0 of every CTA: polls the 256 router logits (lane l takes experts
+// 32 j + l) and the shared-gate coefficient straight into registers, then
+// selects the top 8 in the order of the reference (descending logit, ties to
+// the lower expert index; deltanet.metal:2283-2329): each lane sorts its 8
+// candidates once (19-comparator network on (ordered value, -j) keys), then 8
+// rounds take the largest lane head (warp max, then the lowest expert index
+// among the lanes that hold it) and pop it.  Writes idx[k], the selected
+// (biased) logits sel[k], the 256 biased logits vs[] and *coef.
+__device__ __forceinline__ void topk_poll_select(const uint64_t* ll, uint32_t tag, const float* bias, int lane,
+                                                 int* idx, float* sel, float* vs, float* coef, int* status,
+                                                 int* fail) {
+  const uint64_t* p[9];
+  uint64_t w[9];
+  bool use[9];
+#pragma unroll
+  for (int j = 0; j < 9; j++) {
+    p[j] = j < 8 ? ll + j * 32 + lane : ll + kExperts;
+    use[j] = true;
+    w[j] = ll_get(p[j]);
+  }
+  ll_wait<9>(p, w, use, tag, status, fail);
+  const uint64_t wc = w[8];
+  if (lane == 0) *coef = __uint_as_float(static_cast<uint32_t>(wc));
+  uint64_t c[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int e = j * 32 + lane;
-    v[j] = bias ? __fadd_rn(logits[e], __ldg(bias + e)) : logits[e];
-    vs[e] = v[j];
+    const float lg = __uint_as_float(static_cast<uint32_t>(w[j]));
+    const float v = bias ? __fadd_rn(lg, __ldg(bias + e)) : lg;
+    vs[e] = v;
+    c[j] = (static_cast<uint64_t>(f2ord(v)) << 3) | static_cast<uint64_t>(7 - j);
   }
-  unsigned taken = 0;
+  // sort descending: larger value first, equal values by lower j
+  auto cx = [&](int i0, int i1) {
+    const uint64_t hi = c[i0] > c[i1] ? c[i0] : c[i1];
+    const uint64_t lo = c[i0] > c[i1] ? c[i1] : c[i0];
+    c[i0] = hi;
+    c[i1] = lo;
+  };
+  cx(0, 1); cx(2, 3); cx(4, 5); cx(6, 7);
+  cx(0, 2); cx(1, 3); cx(4, 6); cx(5, 7);
+  cx(1, 2); cx(5, 6); cx(0, 4); cx(3, 7);
+  cx(1, 5); cx(2, 6);
+  cx(1, 4); cx(3, 6);
+  cx(2, 4); cx(3, 5);
+  cx(3, 4);
 #pragma unroll
   for (int k = 0; k < kTopK; k++) {
-    uint32_t best = 0;
-    int bj = 0;
+    const uint32_t key = static_cast<uint32_t>(c[0] >> 3);
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
+    const uint32_t e = (7u - static_cast<uint32_t>(c[0] & 7u)) * 32u + static_cast<uint32_t>(lane);
+    const uint32_t win = __reduce_min_sync(0xffffffffu, key == mx ? e : 0xffffffffu);
+    if (static_cast<int>(win & 31u) == lane) {
 #pragma unroll
-    for (int j = 7; j >= 0; j--) {  // ties within a lane: lower j (lower expert id) wins
-      const uint32_t o = ((taken >> j) & 1u) ? 0u : f2ord(v[j]);
-      if (o >= best) {
-        best = o;
-        bj = j;
-      }
+      for (int j = 0; j < 7; j++) c[j] = c[j + 1];
+      c[7] = 0;
     }
-    const uint32_t mx = __reduce_max_sync(0xffffffffu, best);
-    const uint32_t cand = (best == mx) ? static_cast<uint32_t>(bj * 32 + lane) : 0xffffffffu;
-    const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
-    if (static_cast<int>(win & 31) == lane) taken |= 1u << (win >> 5);
     if (lane == k) {
       idx[k] = static_cast<int>(win);
       sel[k] = ord2f(mx);
@@ -407,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
     if (l == 0) {
       if (tid < kHidden / 8) reinterpret_cast<uint4*>(xh)[tid] = reinterpret_cast<const uint4*>(A.x0)[tid];
     } else {
-      ll_poll(A.ll_h, kHidden + kNOut, tag - 1u, poll, A.status, &m->fail);
+      ll_poll(A.ll_h, kHidden + kNOut, tag - 1u, [&](int i, uint32_t v) { poll[i] = v; }, A.status, &m->fail);
       __syncthreads();
       const float* hv = reinterpret_cast<const float*>(poll);
       if (tid == 0) {
@@ -460,9 +518,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
             ll_put(A.ll_act + (kTopK * kInter + 8 * b + tid) / 2, h2bits(a, a1), tag);
         }
       } else if (b < kNShGu + kNRouter) {
-        if (warp < 8) {
-          const float v = router_row<BF16>(di, warp, xh, lane);
-          if (lane == 0) ll_put(A.ll_logits + 8 * (b - kNShGu) + warp, __float_as_uint(v), tag);
+        // warp w: row w % 8, blocks 4 (w / 8) .. +3; the upper halves travel
+        // through shared memory ([row][block][lane][dot, sum])
+        const int row = warp & 7, h = warp >> 3;
+        float dot[4], sum[4];
+        router_blocks<BF16>(di, row, h, xh, lane, dot, sum);
+        float2* xchg = reinterpret_cast<float2*>(poll);
+        float acc = 0.f;
+        if (h == 1) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) xchg[(row * 4 + i) * 32 + lane] = make_float2(dot[i], sum[i]);
+        } else {
+          acc = router_chain<BF16>(di, row, 0, lane, dot, sum, 0.f);
+        }
+        __syncthreads();
+        if (h == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float2 ds = xchg[(row * 4 + i) * 32 + lane];
+            dot[i] = ds.x;
+            sum[i] = ds.y;
+          }
+          acc = warp_sum(router_chain<BF16>(di, row, 1, lane, dot, sum, acc));
+          if (lane == 0) ll_put(A.ll_logits + 8 * (b - kNShGu) + row, __float_as_uint(acc), tag);
         }
       } else if (warp == 0) {
         const float v = coef_row<BF16>(di, xh, lane);
@@ -471,22 +549,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
     }
 
     // ---------------- phase E: top-k, routed copies, routed gate/up
-    ll_poll(A.ll_logits, kExperts + 1, tag, poll, A.status, &m->fail);
-    __syncthreads();
-    if (m->fail) {
-      drain();
-      return;
-    }
-    if (tid == 0) m->coef = __uint_as_float(poll[kExperts]);
     if (A.r.idx_in) {
+      if (warp == 0) {
+        // only the coefficient is needed from the router words
+        const uint64_t* pc = A.ll_logits + kExperts;
+        uint64_t wc = ll_get(pc);
+        unsigned spins = 0;
+        while (static_cast<uint32_t>(wc >> 32) != tag) {
+          if (++spins > kSpinLimit) {
+            set_status(A.status, kStatusTimeout);
+            m->fail = 1;
+            break;
+          }
+          if (spins > 32) __nanosleep(64);
+          wc = ll_get(pc);
+        }
+        if (lane == 0) m->coef = __uint_as_float(static_cast<uint32_t>(wc));
+      }
       if (tid < kTopK) {
         m->idx[tid] = A.r.idx_in[(size_t)l * kTopK + tid];
         m->w[tid] = A.r.w_in[(size_t)l * kTopK + tid];
       }
     } else if (warp == 0) {
-      topk_select_smem(reinterpret_cast<const float*>(poll), A.r.bias, lane, m->idx, m->w, m->vs);
+      topk_poll_select(A.ll_logits, tag, A.r.bias, lane, m->idx, m->w, m->vs, &m->coef, A.status, &m->fail);
     }
     __syncthreads();
+    if (m->fail) {
+      drain();
+      return;
+    }
     if (tid < kTopK) {
       int rec = A.r.rec_of_pos ? A.r.rec_of_pos[(size_t)l * kTopK + tid] : m->idx[tid];
       if (rec < 0 || (unsigned)rec >= L.bank_records) {
@@ -496,29 +587,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
       m->rec[tid] = rec;
     }
     __syncthreads();
-    {
-      // routed copies: gate/up tile u (two MMA tiles) on rgu[u], then the 8 down
-      // tiles of this CTA's output rows on rdn
-      int t0 = 0;
-      for (int u = 0; u < n_gu; u++) {
-        const int i = b + u * G, k = i >> 5, j = i & 31;
-        const uint8_t* rec = L.bank + static_cast<uint64_t>(m->rec[k]) * L.stride;
-        t0 = copy_gu(routed + (u * 2) * kGuTileBytes, rec, 16 * j, t0);
-        t0 = copy_gu(routed + (u * 2 + 1) * kGuTileBytes, rec, 16 * j + 8, t0);
-        cp_async_arrive(&bars[2 + u]);
-      }
-      if (has_d) {
-        for (int k = 0; k < kTopK; k++)
-          t0 = copy_dn(routed + kMaxGu * 2 * kGuTileBytes + k * kDnTileBytes,
-                       L.bank + static_cast<uint64_t>(m->rec[k]) * L.stride, b, t0);
-        cp_async_arrive(&bars[4]);
-      }
+    // routed copies: gate/up tile u (two MMA tiles) on rgu[u] now; the 8 down
+    // tiles of this CTA's output rows (needed only after the activation
+    // exchange) once the first gate/up tile has landed, so that they do not
+    // share the memory system with the gate/up rows on the critical path
+    for (int u = 0, t0 = 0; u < n_gu; u++) {
+      const int i = b + u * G, k = i >> 5, j = i & 31;
+      const uint8_t* rec = L.bank + static_cast<uint64_t>(m->rec[k]) * L.stride;
+      t0 = copy_gu(routed + (u * 2) * kGuTileBytes, rec, 16 * j, t0);
+      t0 = copy_gu(routed + (u * 2 + 1) * kGuTileBytes, rec, 16 * j + 8, t0);
+      cp_async_arrive(&bars[2 + u]);
     }
-    armed |= (n_gu > 0 ? 4u : 0u) | (n_gu > 1 ? 8u : 0u) | (has_d ? 16u : 0u);
+    armed |= (n_gu > 0 ? 4u : 0u) | (n_gu > 1 ? 8u : 0u);
+    auto issue_dn = [&]() {
+      int t0 = 0;
+      for (int k = 0; k < kTopK; k++)
+        t0 = copy_dn(routed + kMaxGu * 2 * kGuTileBytes + k * kDnTileBytes,
+                     L.bank + static_cast<uint64_t>(m->rec[k]) * L.stride, b, t0);
+      cp_async_arrive(&bars[4]);
+      armed |= 16u;
+    };
+    if (has_d && n_gu == 0) issue_dn();
     // the weights are only needed by the combine: computed while the copies fly
     if (!A.r.idx_in && warp == 1) topk_weights(m->vs, 0, lane, m->w);
     for (int u = 0; u < n_gu; u++) {
       wait_bar(2 + u);
+      if (u == 0 && has_d) issue_dn();
       const int i = b + u * G, k = i >> 5, j = i & 31;
       // warp w: MMA tile w / 8 (row pairs +0 / +8), K-eighth w % 8 (4 groups)
       const unsigned char* tb = routed + (u * 2 + (warp >> 3)) * kGuTileBytes;
@@ -559,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
     if (has_d) {
       float res_v = 0.f;
       if (tid < 16) res_v = (l == 0) ? (A.res0 ? __ldg(A.res0 + 16 * b + tid) : 0.f) : m->res[tid];
-      ll_poll(A.ll_act, kPollWords, tag, poll, A.status, &m->fail);
+      ll_poll(A.ll_act, kActWords, tag, [&](int i, uint32_t v) { poll[i] = v; }, A.status, &m->fail);
       __syncthreads();
       stage_block<true, kThreads>(reinterpret_cast<const __half*>(poll), kDnCols, 8, kInter, kDnCols, afrag, aS,
                                   aC);
@@ -638,7 +732,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 size_t fused1_workspace_bytes() {
   auto a = [](size_t n) { return (n + 255) & ~(size_t)255; };
-  return a(8 * (kExperts + 1)) + a(8 * kPollWords) + a(8 * (kHidden + kNOut));
+  return a(8 * (kExperts + 1)) + a(8 * kActWords) + a(8 * (kHidden + kNOut));
 }
 
 cudaError_t fused1_init_attributes() {
@@ -692,7 +786,7 @@ cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bo
   A.idx_out = idx_out;
   A.w_out = w_out;
   A.ll_logits = reinterpret_cast<uint64_t*>(take(8 * (kExperts + 1)));
-  A.ll_act = reinterpret_cast<uint64_t*>(take(8 * kPollWords));
+  A.ll_act = reinterpret_cast<uint64_t*>(take(8 * kActWords));
   A.ll_h = reinterpret_cast<uint64_t*>(take(8 * (kHidden + kNOut)));
   const size_t ll_bytes = static_cast<size_t>(p - reinterpret_cast<char*>(A.ll_logits));
   // tags restart at 1 every call: clear the words of the previous call

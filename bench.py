@@ -39,6 +39,12 @@ METRIC = "MoE-block tokens/s and achieved HBM GB/s (vs ~8 TB/s) at batch-1 decod
 PREFILL_T = 4096
 EP_T = 16384
 HIDDEN, INTER, TOPK = 2048, 512, 8
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# roofline kernels, from one ncu capture each (profiles/): the one-token decode
+# kernel moves 17.15 MB per layer (4-layer capture, scaled by the layers of a
+# launch); the prefill block's two grouped-GEMM launches move 605 + 512 MB.
+DECODE_TRAFFIC_PER_LAYER = 17.15e6
+PREFILL_GEMM_TRAFFIC = 1117e6
 
 
 def gemm_flops(T: int):
@@ -348,7 +354,7 @@ def main():
                                + uniq[last].sum() * RECORD)
             else:
                 kbytes = float(np.mean((uniq[last] + 1) * GATE_UP_BYTES))
-            res["kernel"] = "k_fused" if prof_kernel == "fused" else "k_gate_up"
+            res["kernel"] = ("k_fused1" if T == 1 else "k_fused") if prof_kernel == "fused" else "k_gate_up"
             res["kernel_ms"] = tot_ms / max(n, 1)
             res["kernel_launches"] = n
             res["kernel_bytes"] = kbytes
@@ -594,7 +600,8 @@ def main():
                 "config": {"workload": f"one MoE block, {pre['T']} tokens, Zipf(1.1) routing"},
                 "kernel_ms": pre["kernel_ms"], "rows_per_expert": pre["rows_per_expert"],
                 "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": tc_peak, "unit": "TFLOP/s",
-                             "frac": gemm_tf / tc_peak, "peak_kind": tc_kind, "traffic": None}}), flush=True)
+                             "frac": gemm_tf / tc_peak, "peak_kind": tc_kind,
+                             "traffic": PREFILL_GEMM_TRAFFIC if pre["T"] == PREFILL_T else None}}), flush=True)
         if dist is not None:
             dist.barrier()
             dist.destroy_process_group()
@@ -641,7 +648,9 @@ def main():
                              "the input rotates over %d token batches" % (head["step_bytes"] / 1e6, POOL)},
             "roofline": {"bound": "hbm", "kernel": head["kernel"], "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind,
+                         "traffic": (DECODE_TRAFFIC_PER_LAYER * args.layers
+                                     if args.batch == 1 and args.prefill_tokens == PREFILL_T else None),
                          "bytes_per_launch": head["kernel_bytes"],
                          "ms_per_launch": head["kernel_ms"]},
             "step_hbm": {"achieved": head["step_gbs"], "frac": head["step_gbs"] / hbm_peak,
@@ -668,7 +677,7 @@ def main():
                              "frac": gemm_tf / tc_peak, "peak_kind": tc_kind,
                              "flops_per_block": pre["routed_gemm_flops"] + pre["shared_gemm_flops"],
                              "routed_only_tflops": routed_tf, "routed_only_frac": routed_tf / tc_peak,
-                             "traffic": None},
+                             "traffic": PREFILL_GEMM_TRAFFIC if pre["T"] == PREFILL_T else None},
             }
         if cst is not None:
             line["cache_stream"] = cache_line(cst)

@@ -375,7 +375,7 @@ __device__ __forceinline__ void topk_poll_select(const uint64_t* ll, uint32_t ta
   cx(1, 4); cx(3, 6);
   cx(2, 4); cx(3, 5);
   cx(3, 4);
-#pragma unroll
+#pragma unroll 1
   for (int k = 0; k < kTopK; k++) {
     const uint32_t key = static_cast<uint32_t>(c[0] >> 3);
     const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
@@ -389,6 +389,63 @@ __device__ __forceinline__ void topk_poll_select(const uint64_t* ll, uint32_t ta
     if (lane == k) {
       idx[k] = static_cast<int>(win);
       sel[k] = ord2f(mx);
+    }
+  }
+}
+
+// Routing weights of the selected 8 (deltanet.metal:2283-2329): softmax over
+// all 256 (biased) logits, renormalised over the 8; same operation order as
+// pk::topk_weights, with lane k computing weight k.  w[k] holds the selected
+// logit on entry and the weight on exit.
+__device__ __forceinline__ void topk_weights1(const float* vs, int lane, float* w) {
+  const float mxv = w[0];
+  float den = 0.f;
+#pragma unroll 1
+  for (int j = 0; j < 8; j++) den = __fadd_rn(den, expf(__fsub_rn(vs[j * 32 + lane], mxv)));
+  den = warp_sum(den);
+  const float p = __fdiv_rn(expf(__fsub_rn(w[lane & 7], mxv)), den);
+  float ps = __shfl_sync(0xffffffffu, p, 0);
+#pragma unroll 1
+  for (int k = 1; k < kTopK; k++) ps = __fadd_rn(ps, __shfl_sync(0xffffffffu, p, k));
+  __syncwarp();
+  if (lane < kTopK) w[lane] = __fdiv_rn(p, ps);
+}
+
+// fp16 vectors as MMA B fragments: pk::stage_block for fp16 sources with the
+// pass loop rolled (this code runs once per layer; see the note on instruction
+// fetch above k_fused1)
+__device__ __forceinline__ void stage_f16(const __half* src, int nvec, int ngrp, int vec_stride, int ncols,
+                                          __half* frag, float* S, float* C) {
+  const int items = nvec * ngrp * 8;
+#pragma unroll 1
+  for (int base = 0; base < items; base += kThreads) {
+    const int item = base + static_cast<int>(threadIdx.x);
+    float s_part = 0.f, c_part = 0.f;
+    int v = 0, g = 0;
+    if (item < items) {
+      v = item / (ngrp * 8);
+      g = (item >> 3) % ngrp;
+      const int q = item & 7;
+      const uint4 hv = *reinterpret_cast<const uint4*>(src + v * vec_stride + g * 64 + q * 8);
+      const __half* h8 = reinterpret_cast<const __half*>(&hv);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int e = q * 8 + j;
+        const __half xh = h8[j];
+        const __half fed = (e & 1) ? __float2half_rn(__half2float(xh) * 0.0625f) : xh;
+        frag[(((size_t)g * ncols + v) * 4 + (e >> 4)) * 16 + frag_half(e)] = fed;
+        s_part += __half2float(xh);
+        c_part += __half2float(fed);
+      }
+    }
+#pragma unroll
+    for (int mm = 1; mm < 8; mm <<= 1) {
+      s_part += __shfl_xor_sync(0xffffffffu, s_part, mm);
+      c_part += __shfl_xor_sync(0xffffffffu, c_part, mm);
+    }
+    if (item < items && (item & 7) == 0) {
+      S[g * ncols + v] = s_part;
+      C[g * ncols + v] = 1024.f * c_part;
     }
   }
 }
@@ -484,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
           __halves2half2(__float2half_rn(__fmul_rn(h4.z, iv)), __float2half_rn(__fmul_rn(h4.w, iv)));
     }
     __syncthreads();
-    stage_block<true, kThreads>(xh, 1, 32, kHidden, 1, xfrag, xS, xC);
+    stage_f16(xh, 1, 32, kHidden, 1, xfrag, xS, xC);
     __syncthreads();
     if (m->fail) {
       drain();
@@ -609,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
     };
     if (has_d && n_gu == 0) issue_dn();
     // the weights are only needed by the combine: computed while the copies fly
-    if (!A.r.idx_in && warp == 1) topk_weights(m->vs, 0, lane, m->w);
+    if (!A.r.idx_in && warp == 1) topk_weights1(m->vs, lane, m->w);
     for (int u = 0; u < n_gu; u++) {
       wait_bar(2 + u);
       if (u == 0 && has_d) issue_dn();
@@ -655,8 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
       if (tid < 16) res_v = (l == 0) ? (A.res0 ? __ldg(A.res0 + 16 * b + tid) : 0.f) : m->res[tid];
       ll_poll(A.ll_act, kActWords, tag, [&](int i, uint32_t v) { poll[i] = v; }, A.status, &m->fail);
       __syncthreads();
-      stage_block<true, kThreads>(reinterpret_cast<const __half*>(poll), kDnCols, 8, kInter, kDnCols, afrag, aS,
-                                  aC);
+      stage_f16(reinterpret_cast<const __half*>(poll), kDnCols, 8, kInter, kDnCols, afrag, aS, aC);
       wait_bar(par);
       wait_bar(4);
       __syncthreads();

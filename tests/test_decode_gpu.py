@@ -133,11 +133,12 @@ def test_block_residual_and_determinism(ctx, layers, oracle_layers):
     assert max_rel(o1.cpu().numpy(), ref["out"]) < TOL
 
 
-def test_block_supplied_routing_and_slot_table(ctx, layers, oracle_layers):
+@pytest.mark.parametrize("T", [1, 6])
+def test_block_supplied_routing_and_slot_table(ctx, layers, oracle_layers, T):
     """Routing supplied by the oracle; records addressed through a permuted slot arena
-    (the cache's slot_indices, deltanet.metal:2155-2211)."""
+    (the cache's slot_indices, deltanet.metal:2155-2211).  T = 1 runs the one-token
+    kernel, T = 6 the T <= 8 persistent kernel."""
     from qfmoe import block_forward
-    T = 6
     x = hidden(T, tok0=300)
     rng = np.random.default_rng(5)
     idx = np.stack([rng.choice(256, 8, replace=False) for _ in range(T)]).astype(np.int32)
@@ -164,9 +165,46 @@ def test_block_supplied_routing_and_slot_table(ctx, layers, oracle_layers):
     assert max_rel(out.cpu().numpy(), ref["out"]) < TOL
 
 
-def test_block_logit_bias(ctx, layers, oracle_layers):
+@pytest.mark.parametrize("T", [1, 3])
+def test_block_router_ties_go_to_the_lower_index(ctx, layers, T):
+    """Exact logit ties through the whole block: router rows duplicated so that a
+    lower-index copy of token 0's top expert ties with it (it must rank just
+    before it) and a higher-index copy of the 8th expert ties with that one (it
+    must lose the last place), as the reference's strict-> scan orders them
+    (deltanet.metal:2283-2329).  T = 1 runs the one-token kernel's top-8."""
+    from qfmoe import MoELayerWeights, block_forward
+    x = hidden(T, tok0=31)
+    rw, rs, rb = (a.copy() for a in O.synth_router(SEED, 0))
+    coef = O.synth_coef(SEED, 0)
+    shared = O.synth_record(SEED, 0, 256)
+    lg, _ = O.router(O.OracleLayer((rw, rs, rb), coef, shared, {}), x.numpy().view(np.uint16)[:1])
+    order = [int(e) for e in np.argsort(-lg[0], kind="stable")]
+    top = order[0]
+    lo = next((e for e in range(top) if e not in order[:8]), None)
+    # the expert that ranks 8th once the copy of the top expert takes a place
+    eighth = order[6] if lo is not None else order[7]
+    hi = next(e for e in range(eighth + 1, 256) if e not in order[:8])
+    W, S, B = rw.reshape(256, -1), rs.reshape(256, -1), rb.reshape(256, -1)
+    for src, dst in ([(top, lo)] if lo is not None else []) + [(eighth, hi)]:
+        W[dst], S[dst], B[dst] = W[src], S[src], B[src]
+    OL = O.OracleLayer((rw, rs, rb), coef, shared, {e: O.synth_record(SEED, 0, e) for e in range(256)})
+    ref = O.block(OL, x.numpy().view(np.uint16), threads=8)
+    if lo is not None:
+        assert list(ref["idx"][0, :2]) == [lo, top]
+    assert hi not in ref["idx"][0] and eighth in ref["idx"][0]
+    L = layers[(0, False)]
+    Lt = MoELayerWeights(torch.from_numpy(rw).cuda(), torch.from_numpy(rs.view(np.int16)).cuda(),
+                         torch.from_numpy(rb.view(np.int16)).cuda(), L.coef_w, L.coef_s, L.coef_b,
+                         L.shared, L.bank)
+    out, idx, _ = block_forward(ctx, Lt, x.cuda(), return_routing=True)
+    ctx.check()
+    assert np.array_equal(idx.cpu().numpy(), ref["idx"])
+    assert max_rel(out.cpu().numpy(), ref["out"]) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_block_logit_bias(ctx, layers, oracle_layers, T):
     from qfmoe import block_forward
-    T = 16
     x = hidden(T, tok0=900)
     bias = (np.log(1.0 / np.arange(1, 257) ** 1.1) * 2.0).astype(np.float32)
     out, idx, _ = block_forward(ctx, layers[(0, False)], x.cuda(),

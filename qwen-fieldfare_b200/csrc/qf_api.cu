@@ -225,6 +225,16 @@ qf_status qf_moe_dispatch_plan(qf_moe* h, const int32_t* idx, int32_t T, int32_t
   return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_dispatch_plan");
 }
 
+namespace {
+size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+// grouped path for a stack of T = 9..64 tokens: fp32 h and fp16 x ping-pong
+// buffers, then one block's grouped-path workspace
+size_t grouped_stack_bytes(int T) {
+  const size_t th = static_cast<size_t>(T) * qf::kHidden;
+  return 2 * al256(4 * th) + 2 * al256(2 * th) + qf::prefill_workspace_bytes(T);
+}
+}  // namespace
+
 qf_status qf_moe_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
   if (!h || !bytes) return QF_ERR_ARG;
   if (T < 1 || T > qf::kPrefillMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
@@ -233,7 +243,7 @@ qf_status qf_moe_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
     return QF_OK;
   }
   const size_t a = qf::decode_workspace_bytes(T);
-  const size_t b = T <= qf::kFusedMaxTokens ? qf::fused_workspace_bytes(T) : 0;
+  const size_t b = T <= qf::kFusedMaxTokens ? qf::fused_workspace_bytes(T) : grouped_stack_bytes(T);
   *bytes = a > b ? a : b;
   return QF_OK;
 }
@@ -268,6 +278,9 @@ qf_status qf_moe_block_forward(qf_moe* h, const qf_moe_layer* layer, int32_t T, 
       return fail(h, QF_ERR_ARG, "workspace too small");
     e = qf::fused_stack(stream_of(h), &w, 1, bf16, T, x, residual, out, 1e-6f, r, idx_out, w_out,
                         workspace, h->d_status, &h->prof);
+  } else if (T >= qf::kGroupedMinTokens && w.bank_records >= (uint32_t)qf::kExperts && !r.rec_of_pos) {
+    e = qf::prefill_block(stream_of(h), w, bf16, T, x, residual, out, r, idx_out, w_out, workspace,
+                          h->d_status, &h->prof);
   } else {
     qf::DecodeWs ws;
     qf::decode_carve(workspace, T, &ws);
@@ -305,9 +318,32 @@ qf_status qf_moe_stack_forward(qf_moe* h, const qf_moe_layer* layers, int32_t n_
                                     eps, r, idx_out, w_out, workspace, h->d_status, &h->prof);
     return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_stack_forward");
   }
+  const size_t PT = static_cast<size_t>(T) * qf::kTopK;
+  bool resident = T >= qf::kGroupedMinTokens;
+  for (int l = 0; l < n_layers && resident; l++) resident = lw[l].bank_records >= (uint32_t)qf::kExperts;
+  if (resident) {
+    // grouped path per block, RMSNorm between blocks (same order as the decode kernels)
+    const size_t th = static_cast<size_t>(T) * qf::kHidden;
+    char* p = static_cast<char*>(workspace);
+    float* hb[2] = {reinterpret_cast<float*>(p), reinterpret_cast<float*>(p + al256(4 * th))};
+    p += 2 * al256(4 * th);
+    uint16_t* xb[2] = {reinterpret_cast<uint16_t*>(p), reinterpret_cast<uint16_t*>(p + al256(2 * th))};
+    p += 2 * al256(2 * th);
+    for (int l = 0; l < n_layers; l++) {
+      const int cur = l & 1;
+      const uint16_t* xin = (l == 0) ? x : xb[cur];
+      const float* res = (l == 0) ? residual : hb[cur];
+      float* o = (l == n_layers - 1) ? out : hb[cur ^ 1];
+      cudaError_t e = qf::prefill_block(stream_of(h), lw[l], bf16, T, xin, res, o, r,
+                                        idx_out ? idx_out + l * PT : nullptr,
+                                        w_out ? w_out + l * PT : nullptr, p, h->d_status, &h->prof);
+      if (e == cudaSuccess && l + 1 < n_layers) e = qf::rmsnorm_f16(stream_of(h), T, o, eps, xb[cur ^ 1]);
+      if (e != cudaSuccess) return cuda_fail(h, e, "qf_moe_stack_forward");
+    }
+    return QF_OK;
+  }
   qf::DecodeWs ws;
   qf::decode_carve(workspace, T, &ws);
-  const size_t PT = static_cast<size_t>(T) * qf::kTopK;
   for (int l = 0; l < n_layers; l++) {
     const int cur = l & 1;
     const uint16_t* xin = (l == 0) ? x : ws.x16[cur];

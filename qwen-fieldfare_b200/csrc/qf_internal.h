@@ -118,6 +118,11 @@ size_t prefill_workspace_bytes(int T);
 cudaError_t prefill_init_attributes();
 cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
                                   const uint16_t* x, float* logits, float* coef);
+// T = 9..64 with a resident bank also takes the grouped path (its tcgen05
+// GEMMs stream the routed weights faster than the per-kernel decode path).
+constexpr int kGroupedMinTokens = 9;
+// x16 = fp16(RMSNorm(h)) per token (stack transition of the grouped path)
+cudaError_t rmsnorm_f16(cudaStream_t st, int T, const float* h, float eps, uint16_t* x16);
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
                           float* w_out, void* workspace, int* status, Prof* prof);

@@ -950,6 +950,39 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
   return cudaGetLastError();
 }
 
+// RMSNorm of the stack transition (deltanet.metal:18-53, unit weight) for the
+// grouped path: x16 = fp16(h / rms(h)) per token, the mean of squares summed as
+// 128 tiles of 16 rows (fma chain inside a tile, tiles summed in order), the
+// order of the decode kernels and the oracle.  One CTA (128 threads) per token.
+__global__ void __launch_bounds__(128) k_rmsnorm_f16(const float* __restrict__ h, float eps,
+                                                      uint16_t* __restrict__ x16) {
+  __shared__ float part[128];
+  __shared__ float inv;
+  const float* v = h + (size_t)blockIdx.x * kHidden;
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    const float e = v[threadIdx.x * 16 + j];
+    acc = __fmaf_rn(e, e, acc);
+  }
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int c = 0; c < 128; c++) tot = __fadd_rn(tot, part[c]);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)kHidden), eps)));
+  }
+  __syncthreads();
+  const float iv = inv;
+  __half* o = reinterpret_cast<__half*>(x16) + (size_t)blockIdx.x * kHidden;
+  for (int i = threadIdx.x; i < kHidden; i += 128) o[i] = __float2half_rn(__fmul_rn(v[i], iv));
+}
+
+cudaError_t rmsnorm_f16(cudaStream_t st, int T, const float* h, float eps, uint16_t* x16) {
+  k_rmsnorm_f16<<<T, 128, 0, st>>>(h, eps, x16);
+  return cudaGetLastError();
+}
+
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
                           float* w_out, void* workspace, int* status, Prof* prof) {

@@ -133,11 +133,12 @@ def test_block_residual_and_determinism(ctx, layers, oracle_layers):
     assert max_rel(o1.cpu().numpy(), ref["out"]) < TOL
 
 
-@pytest.mark.parametrize("T", [1, 6])
+@pytest.mark.parametrize("T", [1, 6, 20])
 def test_block_supplied_routing_and_slot_table(ctx, layers, oracle_layers, T):
     """Routing supplied by the oracle; records addressed through a permuted slot arena
     (the cache's slot_indices, deltanet.metal:2155-2211).  T = 1 runs the one-token
-    kernel, T = 6 the T <= 8 persistent kernel."""
+    kernel, T = 6 the T <= 8 persistent kernel, T = 20 the per-kernel decode path
+    (a slot arena keeps T = 9..64 off the grouped path)."""
     from qfmoe import block_forward
     x = hidden(T, tok0=300)
     rng = np.random.default_rng(5)
@@ -232,7 +233,8 @@ def test_stack_equals_chained_blocks_with_oracle_norm(ctx, layers, oracle_layers
     """Two stacked blocks == block 0, the oracle's RMSNorm of its output, block 1:
     bitwise, which pins the in-kernel RMSNorm (deltanet.metal:18-53) to the oracle.
     T = 1 runs the one-token persistent kernel, T = 3 the T <= 8 persistent
-    kernel, T = 12 the per-kernel path."""
+    kernel, T = 12 the grouped tcgen05 path with the RMSNorm kernel between
+    blocks."""
     from qfmoe import StackPlan, block_forward, stack_forward
     x = hidden(T, tok0=40)
     plan = StackPlan([layers[(0, False)], layers[(1, False)]])

@@ -1015,8 +1015,11 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   if (e != cudaSuccess) return e;
 
   {
+    // decode batches (T <= 64): the decode router spreads over row blocks x
+    // token chunks; both are bit-exact in the reference lane order
     ProfScope ps(prof, kKRouter, st);
-    e = router_logits_prefill(st, L, bf16, T, x, logits, coef);
+    e = T <= kDecodeMaxTokens ? router_logits(st, L, bf16, T, x, logits, coef, status)
+                              : router_logits_prefill(st, L, bf16, T, x, logits, coef);
   }
   if (e != cudaSuccess) return e;
   if (r.idx_in) {

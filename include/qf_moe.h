@@ -152,10 +152,11 @@ qf_status qf_moe_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
  *   x: fp16 [T * hidden] post-norm hidden; residual: fp32 [T * hidden] or NULL;
  *   out: fp32 [T * hidden]; idx_out/w_out: optional [T * top_k];
  *   routing: optional; workspace: >= qf_moe_workspace_size bytes (256-B aligned).
- * T in [1, 8] runs one persistent cooperative kernel (all phases of the block,
- * grid barriers between them); T in [9, 64] runs five kernels per block;
- * T in [65, 32768] (prefill) runs the grouped tensor-core path, which needs a
- * bank of all 256 experts (bank_records >= 256) and no record_of_pos. */
+ * T = 1 runs the one-token persistent kernel (no grid barriers: vectors cross
+ * CTAs as tagged words); T in [2, 8] a persistent kernel with grid barriers.
+ * T in [9, 32768] runs the grouped tensor-core path when the bank holds all
+ * 256 experts (bank_records >= 256) and there is no record_of_pos; otherwise
+ * T in [9, 64] runs five kernels per block and T > 64 is rejected. */
 qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
                                const uint16_t *x, const float *residual, float *out,
                                const qf_routing *routing, int32_t *idx_out, float *w_out,
@@ -165,7 +166,9 @@ qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
  * runner :958).  Layer l reads x_l (fp16) and residual h_l; writes
  * h_{l+1} = out_l; x_{l+1} = fp16(RMSNorm(out_l)) with unit weight and `eps`
  * (qwen_rmsnorm_f32, deltanet.metal:18-53).  `layers` is a HOST array of
- * n_layers descriptors.  idx_out/w_out (optional): [n_layers * T * top_k]. */
+ * n_layers descriptors.  idx_out/w_out (optional): [n_layers * T * top_k].
+ * T in [1, 8]: the whole stack is one persistent launch; T in [9, 64]: one
+ * block at a time (grouped path for resident banks) with the RMSNorm between. */
 qf_status qf_moe_stack_forward(qf_moe *h, const qf_moe_layer *layers, int32_t n_layers,
                                int32_t T, const uint16_t *x, const float *residual, float *out,
                                float eps, int32_t *idx_out, float *w_out, void *workspace,

@@ -383,6 +383,109 @@ __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restric
   if (e == 0) *n_tiles = total_full + n_part;
 }
 
+// ------------------------------------------------------------------ small-T plan
+// T <= 64 (at most 512 routed positions) in ONE CTA: the copies of the routing
+// to idx_out / w_out, the per-expert counts and offsets, the stable
+// permutation by (expert, position) and the tile list -- the same results as
+// dispatch_plan_ws + k_tile_list, whose logic it repeats for a single chunk,
+// without four launches and two copies per block.
+constexpr int kPlanSmallThreads = 512;
+__global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
+    const int* __restrict__ idx, const float* __restrict__ w, int T, int* __restrict__ idx_out,
+    float* __restrict__ w_out, int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ perm,
+    int4* __restrict__ tiles, int* __restrict__ n_tiles, int* status) {
+  __shared__ int h[kExperts];
+  __shared__ int excl[kExperts + 1];
+  __shared__ int wh[kPlanSmallThreads / 32][kExperts];  // per-warp counts, then prefix
+  __shared__ int s_rem[kListThreads];
+  __shared__ int s_warp[kListThreads / 32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = T * kTopK;
+  for (int i = tid; i < kExperts; i += blockDim.x) h[i] = 0;
+  for (int i = tid; i < (kPlanSmallThreads / 32) * kExperts; i += blockDim.x) (&wh[0][0])[i] = 0;
+  __syncthreads();
+  int e = -1;
+  if (tid < n) {
+    e = idx[tid];
+    if (idx_out) idx_out[tid] = e;
+    if (w_out) w_out[tid] = w[tid];
+    if (e >= 0 && e < kExperts) {
+      atomicAdd(&h[e], 1);
+    } else {
+      set_status(status, kStatusDevice);
+      e = -1;
+    }
+  }
+  // rank among equal experts inside the warp, per-warp counts
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) wh[warp][e] = __popc(peers);
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int i = 0; i < kExperts; i++) {
+      excl[i] = acc;
+      acc += h[i];
+    }
+    excl[kExperts] = acc;
+  }
+  for (int x = tid; x < kExperts; x += blockDim.x) {
+    int acc = 0;
+    for (int q = 0; q < kPlanSmallThreads / 32; q++) {
+      const int c = wh[q][x];
+      wh[q][x] = acc;
+      acc += c;
+    }
+  }
+  __syncthreads();
+  for (int x = tid; x <= kExperts; x += blockDim.x) {
+    if (x < kExperts) counts[x] = h[x];
+    offsets[x] = excl[x];
+  }
+  if (e >= 0) perm[excl[e] + wh[warp][e] + rank] = tid;
+  // tile list (k_tile_list): threads 0..287, expert 256 = the shared expert
+  int cnt = 0, base = 0;
+  if (tid < kExperts) {
+    cnt = h[tid];
+    base = excl[tid];
+  } else if (tid == kExperts) {
+    cnt = T;
+    base = T * kTopK;
+  }
+  const int full = cnt / kTileRows, rem = cnt % kTileRows;
+  if (tid < kListThreads) s_rem[tid] = rem;
+  int v = full;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
+  }
+  if (tid < kListThreads && lane == 31) s_warp[warp] = v;
+  __syncthreads();
+  int n_part = 0;
+  if (tid < kListThreads) {
+    int before = 0, total_full = 0;
+    for (int q = 0; q < kListThreads / 32; q++) {
+      const int sw = s_warp[q];
+      if (q < warp) before += sw;
+      total_full += sw;
+    }
+    const int first = before + v - full;
+    for (int j = 0; j < full; j++) tiles[first + j] = make_int4(tid, j * kTileRows, kTileRows, base);
+    if (rem > 0) {
+      int pos = 0;
+      for (int o = 0; o < kListThreads; o++) {
+        const int r2 = s_rem[o];
+        pos += (r2 > rem || (r2 == rem && o < tid)) ? 1 : 0;
+      }
+      tiles[total_full + pos] = make_int4(tid, full * kTileRows, rem, base);
+    }
+    n_part = total_full;  // carried for thread 0 below
+  }
+  const int parts = __syncthreads_count(tid < kListThreads && rem > 0);
+  if (tid == 0) *n_tiles = n_part + parts;
+}
+
 // ------------------------------------------------------------------ grouped GEMM
 // Work unit = (tile of <= 128 token rows of one expert, two 128-row weight
 // blocks sharing that token tile): gate rows f0..f0+127 and up rows
@@ -1031,12 +1134,17 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
     e = router_topk(st, T, logits, r.bias, idx, w, status);
   }
   if (e != cudaSuccess) return e;
-  if (idx_out) e = cudaMemcpyAsync(idx_out, idx, 4 * P, cudaMemcpyDeviceToDevice, st);
-  if (e == cudaSuccess && w_out) e = cudaMemcpyAsync(w_out, w, 4 * P, cudaMemcpyDeviceToDevice, st);
-  if (e != cudaSuccess) return e;
-  e = dispatch_plan_ws(st, idx, T, counts, offsets, perm, plan_ws, status);
-  if (e != cudaSuccess) return e;
-  k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, nullptr, tiles, n_tiles);
+  if (T <= kDecodeMaxTokens) {
+    k_plan_small<<<1, kPlanSmallThreads, 0, st>>>(idx, w, T, idx_out, w_out, counts, offsets, perm, tiles,
+                                                 n_tiles, status);
+  } else {
+    if (idx_out) e = cudaMemcpyAsync(idx_out, idx, 4 * P, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess && w_out) e = cudaMemcpyAsync(w_out, w, 4 * P, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return e;
+    e = dispatch_plan_ws(st, idx, T, counts, offsets, perm, plan_ws, status);
+    if (e != cudaSuccess) return e;
+    k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, nullptr, tiles, n_tiles);
+  }
   k_gather_rows<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(perm, (int)P, T, reinterpret_cast<const uint4*>(x),
                                                           reinterpret_cast<uint4*>(xs));
   e = grouped_ffn(st, L, bf16, xs, R, act, y, perm, tiles, n_tiles, max_tiles, sms, status, prof, nullptr);

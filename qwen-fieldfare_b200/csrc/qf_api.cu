@@ -322,7 +322,8 @@ qf_status qf_moe_stack_forward(qf_moe* h, const qf_moe_layer* layers, int32_t n_
   bool resident = T >= qf::kGroupedMinTokens;
   for (int l = 0; l < n_layers && resident; l++) resident = lw[l].bank_records >= (uint32_t)qf::kExperts;
   if (resident) {
-    // grouped path per block, RMSNorm between blocks (same order as the decode kernels)
+    // grouped path per block; its combine also writes the next block's RMSNorm
+    // input (same order as the decode kernels)
     const size_t th = static_cast<size_t>(T) * qf::kHidden;
     char* p = static_cast<char*>(workspace);
     float* hb[2] = {reinterpret_cast<float*>(p), reinterpret_cast<float*>(p + al256(4 * th))};
@@ -336,8 +337,8 @@ qf_status qf_moe_stack_forward(qf_moe* h, const qf_moe_layer* layers, int32_t n_
       float* o = (l == n_layers - 1) ? out : hb[cur ^ 1];
       cudaError_t e = qf::prefill_block(stream_of(h), lw[l], bf16, T, xin, res, o, r,
                                         idx_out ? idx_out + l * PT : nullptr,
-                                        w_out ? w_out + l * PT : nullptr, p, h->d_status, &h->prof);
-      if (e == cudaSuccess && l + 1 < n_layers) e = qf::rmsnorm_f16(stream_of(h), T, o, eps, xb[cur ^ 1]);
+                                        w_out ? w_out + l * PT : nullptr, p, h->d_status, &h->prof,
+                                        l + 1 < n_layers ? xb[cur ^ 1] : nullptr, eps);
       if (e != cudaSuccess) return cuda_fail(h, e, "qf_moe_stack_forward");
     }
     return QF_OK;

@@ -193,69 +193,6 @@ __global__ void __launch_bounds__(kThreads) k_router(LayerW L, int T,
   }
 }
 
-// ---------------------------------------------------------------- top-k
-// Warp-parallel selection of the top-8 logits of one token: 8 rounds of a
-// (value desc, index asc) warp argmax, which orders ties exactly like the
-// reference's strict-> insertion scan.
-__device__ __forceinline__ void topk_token(int t, const float* __restrict__ logits,
-                                           const float* __restrict__ bias, int* __restrict__ idx,
-                                           float* __restrict__ w, int lane) {
-  float v[8];
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int e = j * 32 + lane;
-    const float l = logits[static_cast<size_t>(t) * kExperts + e];
-    v[j] = bias ? __fadd_rn(l, bias[e]) : l;
-  }
-  unsigned taken = 0;
-  float selv[kTopK];
-  int seli[kTopK];
-#pragma unroll
-  for (int k = 0; k < kTopK; k++) {
-    float bv = -INFINITY;
-    int bix = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const int e = j * 32 + lane;
-      if (!((taken >> j) & 1u) && (v[j] > bv || (v[j] == bv && e < bix))) {
-        bv = v[j];
-        bix = e;
-      }
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
-      const int oi = __shfl_xor_sync(0xffffffffu, bix, m);
-      if (ov > bv || (ov == bv && oi < bix)) {
-        bv = ov;
-        bix = oi;
-      }
-    }
-    selv[k] = bv;
-    seli[k] = bix;
-    if ((bix & 31) == lane) taken |= 1u << (bix >> 5);
-  }
-  const float mx = selv[0];
-  float den = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; j++) den = __fadd_rn(den, expf(__fsub_rn(v[j], mx)));
-  den = warp_sum(den);
-  float p[kTopK];
-  float ps = 0.f;
-#pragma unroll
-  for (int k = 0; k < kTopK; k++) {
-    p[k] = __fdiv_rn(expf(__fsub_rn(selv[k], mx)), den);
-    ps = __fadd_rn(ps, p[k]);
-  }
-#pragma unroll
-  for (int k = 0; k < kTopK; k++) {
-    if (lane == k) {
-      idx[t * kTopK + k] = seli[k];
-      w[t * kTopK + k] = __fdiv_rn(p[k], ps);
-    }
-  }
-}
-
 __global__ void __launch_bounds__(1024) k_topk(int T, const float* __restrict__ logits,
                                                const float* __restrict__ bias, int* idx, float* w) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;

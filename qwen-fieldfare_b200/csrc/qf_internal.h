@@ -121,11 +121,11 @@ cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, i
 // T = 9..64 with a resident bank also takes the grouped path (its tcgen05
 // GEMMs stream the routed weights faster than the per-kernel decode path).
 constexpr int kGroupedMinTokens = 9;
-// x16 = fp16(RMSNorm(h)) per token (stack transition of the grouped path)
-cudaError_t rmsnorm_f16(cudaStream_t st, int T, const float* h, float eps, uint16_t* x16);
+// x16_next (optional): fp16 RMSNorm(out) with `eps` for a following block
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
-                          float* w_out, void* workspace, int* status, Prof* prof);
+                          float* w_out, void* workspace, int* status, Prof* prof,
+                          uint16_t* x16_next = nullptr, float eps = 0.f);
 
 // grouped expert FFN over a row space (qf_prefill.cu): tiles of <= 128 rows per
 // expert from counts/offsets (expert 256 = the shared expert over T_shared rows

@@ -384,16 +384,20 @@ __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restric
 }
 
 // ------------------------------------------------------------------ small-T plan
-// T <= 64 (at most 512 routed positions) in ONE CTA: the copies of the routing
-// to idx_out / w_out, the per-expert counts and offsets, the stable
+// T <= 64 (at most 512 routed positions) in ONE CTA: top-8 of every token
+// (topk_token, one token per warp; logits == nullptr when idx / w already hold
+// the routing), or the copy of the supplied routing, then the copies of the
+// routing to idx_out / w_out, the per-expert counts and offsets, the stable
 // permutation by (expert, position) and the tile list -- the same results as
-// dispatch_plan_ws + k_tile_list, whose logic it repeats for a single chunk,
-// without four launches and two copies per block.
-constexpr int kPlanSmallThreads = 512;
+// k_topk + dispatch_plan_ws + k_tile_list, whose logic it repeats for a single
+// chunk, without five launches and two copies per block.
+constexpr int kPlanSmallThreads = 1024;
+constexpr int kPlanTopkMaxTokens = kPlanSmallThreads / 32;
 __global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
-    const int* __restrict__ idx, const float* __restrict__ w, int T, int* __restrict__ idx_out,
-    float* __restrict__ w_out, int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ perm,
-    int4* __restrict__ tiles, int* __restrict__ n_tiles, int* status) {
+    const float* __restrict__ logits, const float* __restrict__ bias, const int* __restrict__ idx_in,
+    const float* __restrict__ w_in, int* __restrict__ idx, float* __restrict__ w, int T,
+    int* __restrict__ idx_out, float* __restrict__ w_out, int* __restrict__ counts, int* __restrict__ offsets,
+    int* __restrict__ perm, int4* __restrict__ tiles, int* __restrict__ n_tiles, int* status) {
   __shared__ int h[kExperts];
   __shared__ int excl[kExperts + 1];
   __shared__ int wh[kPlanSmallThreads / 32][kExperts];  // per-warp counts, then prefix
@@ -401,6 +405,15 @@ __global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
   __shared__ int s_warp[kListThreads / 32];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = T * kTopK;
+  if (idx_in) {
+    if (tid < n) {
+      idx[tid] = idx_in[tid];
+      w[tid] = w_in[tid];
+    }
+  } else if (logits) {
+    if (warp < T) topk_token(warp, logits, bias, idx, w, lane);
+  }
+  __syncthreads();
   for (int i = tid; i < kExperts; i += blockDim.x) h[i] = 0;
   for (int i = tid; i < (kPlanSmallThreads / 32) * kExperts; i += blockDim.x) (&wh[0][0])[i] = 0;
   __syncthreads();
@@ -852,12 +865,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
 
 // out = (residual + sigmoid(c) * shared) + sum_k w_k * y_k, the products
 // rounded and summed in router order (deltanet.metal:2213-2227)
+// x16_next (optional): fp16 RMSNorm of the output row for a following block
+// (deltanet.metal:18-53, unit weight): the mean of squares summed as 128 tiles
+// of 16 rows (fma chain inside a tile, tiles summed in order), the order of the
+// decode kernels and the oracle, so stacked blocks equal chained ones bit for bit
 __global__ void __launch_bounds__(256) k_combine_weighted(int T, const float* __restrict__ residual,
                                                           const float* __restrict__ y_pos,
                                                           const float* __restrict__ w,
                                                           const float* __restrict__ y_sh,
                                                           const float* __restrict__ coef,
-                                                          float* __restrict__ out) {
+                                                          float* __restrict__ out, float eps,
+                                                          uint16_t* __restrict__ x16_next) {
+  __shared__ float vrow[kHidden];
+  __shared__ float part[kHidden / 16];
+  __shared__ float inv;
   const int t = blockIdx.x;
   const float c = coef[t];
   const float coeff = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-c)));
@@ -881,11 +902,33 @@ __global__ void __launch_bounds__(256) k_combine_weighted(int T, const float* __
     }
     const float4 sh = s4[i];
     const float4 base = r4 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    o4[i] = make_float4(__fadd_rn(__fadd_rn(base.x, __fmul_rn(sh.x, coeff)), acc.x),
-                        __fadd_rn(__fadd_rn(base.y, __fmul_rn(sh.y, coeff)), acc.y),
-                        __fadd_rn(__fadd_rn(base.z, __fmul_rn(sh.z, coeff)), acc.z),
-                        __fadd_rn(__fadd_rn(base.w, __fmul_rn(sh.w, coeff)), acc.w));
+    const float4 v = make_float4(__fadd_rn(__fadd_rn(base.x, __fmul_rn(sh.x, coeff)), acc.x),
+                                 __fadd_rn(__fadd_rn(base.y, __fmul_rn(sh.y, coeff)), acc.y),
+                                 __fadd_rn(__fadd_rn(base.z, __fmul_rn(sh.z, coeff)), acc.z),
+                                 __fadd_rn(__fadd_rn(base.w, __fmul_rn(sh.w, coeff)), acc.w));
+    o4[i] = v;
+    if (x16_next) reinterpret_cast<float4*>(vrow)[i] = v;
   }
+  if (!x16_next) return;
+  __syncthreads();
+  if (threadIdx.x < kHidden / 16) {
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const float e = vrow[threadIdx.x * 16 + j];
+      a = __fmaf_rn(e, e, a);
+    }
+    part[threadIdx.x] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int c2 = 0; c2 < kHidden / 16; c2++) tot = __fadd_rn(tot, part[c2]);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)kHidden), eps)));
+  }
+  __syncthreads();
+  __half* o = reinterpret_cast<__half*>(x16_next) + (size_t)t * kHidden;
+  for (int i = threadIdx.x; i < kHidden; i += 256) o[i] = __float2half_rn(__fmul_rn(vrow[i], inv));
 }
 
 }  // namespace
@@ -1053,42 +1096,10 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
   return cudaGetLastError();
 }
 
-// RMSNorm of the stack transition (deltanet.metal:18-53, unit weight) for the
-// grouped path: x16 = fp16(h / rms(h)) per token, the mean of squares summed as
-// 128 tiles of 16 rows (fma chain inside a tile, tiles summed in order), the
-// order of the decode kernels and the oracle.  One CTA (128 threads) per token.
-__global__ void __launch_bounds__(128) k_rmsnorm_f16(const float* __restrict__ h, float eps,
-                                                      uint16_t* __restrict__ x16) {
-  __shared__ float part[128];
-  __shared__ float inv;
-  const float* v = h + (size_t)blockIdx.x * kHidden;
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < 16; j++) {
-    const float e = v[threadIdx.x * 16 + j];
-    acc = __fmaf_rn(e, e, acc);
-  }
-  part[threadIdx.x] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int c = 0; c < 128; c++) tot = __fadd_rn(tot, part[c]);
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)kHidden), eps)));
-  }
-  __syncthreads();
-  const float iv = inv;
-  __half* o = reinterpret_cast<__half*>(x16) + (size_t)blockIdx.x * kHidden;
-  for (int i = threadIdx.x; i < kHidden; i += 128) o[i] = __float2half_rn(__fmul_rn(v[i], iv));
-}
-
-cudaError_t rmsnorm_f16(cudaStream_t st, int T, const float* h, float eps, uint16_t* x16) {
-  k_rmsnorm_f16<<<T, 128, 0, st>>>(h, eps, x16);
-  return cudaGetLastError();
-}
-
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           const float* residual, float* out, const RoutingArgs& r, int* idx_out,
-                          float* w_out, void* workspace, int* status, Prof* prof) {
+                          float* w_out, void* workspace, int* status, Prof* prof, uint16_t* x16_next,
+                          float eps) {
   const size_t P = static_cast<size_t>(T) * kTopK;
   const size_t R = P + static_cast<size_t>(T);
   const size_t max_tiles = max_tiles_for(T);
@@ -1125,19 +1136,29 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
                               : router_logits_prefill(st, L, bf16, T, x, logits, coef);
   }
   if (e != cudaSuccess) return e;
-  if (r.idx_in) {
-    e = cudaMemcpyAsync(idx, r.idx_in, 4 * P, cudaMemcpyDeviceToDevice, st);
-    if (e != cudaSuccess) return e;
-    e = cudaMemcpyAsync(w, r.w_in, 4 * P, cudaMemcpyDeviceToDevice, st);
-  } else {
-    ProfScope ps(prof, kKTopk, st);
-    e = router_topk(st, T, logits, r.bias, idx, w, status);
-  }
-  if (e != cudaSuccess) return e;
   if (T <= kDecodeMaxTokens) {
-    k_plan_small<<<1, kPlanSmallThreads, 0, st>>>(idx, w, T, idx_out, w_out, counts, offsets, perm, tiles,
-                                                 n_tiles, status);
+    // above one token per warp the plan CTA's top-k costs more than its own launch
+    const bool own_topk = !r.idx_in && T > kPlanTopkMaxTokens;
+    if (own_topk) {
+      ProfScope ps(prof, kKTopk, st);
+      e = router_topk(st, T, logits, r.bias, idx, w, status);
+      if (e != cudaSuccess) return e;
+    }
+    // timed as the top-k kernel when it selects the top-8 itself
+    ProfScope ps(prof, own_topk || r.idx_in ? -2 : kKTopk, st);  // -2: never timed
+    k_plan_small<<<1, kPlanSmallThreads, 0, st>>>(own_topk ? nullptr : logits, r.bias, r.idx_in, r.w_in, idx,
+                                                 w, T, idx_out, w_out, counts, offsets, perm, tiles, n_tiles,
+                                                 status);
   } else {
+    if (r.idx_in) {
+      e = cudaMemcpyAsync(idx, r.idx_in, 4 * P, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return e;
+      e = cudaMemcpyAsync(w, r.w_in, 4 * P, cudaMemcpyDeviceToDevice, st);
+    } else {
+      ProfScope ps(prof, kKTopk, st);
+      e = router_topk(st, T, logits, r.bias, idx, w, status);
+    }
+    if (e != cudaSuccess) return e;
     if (idx_out) e = cudaMemcpyAsync(idx_out, idx, 4 * P, cudaMemcpyDeviceToDevice, st);
     if (e == cudaSuccess && w_out) e = cudaMemcpyAsync(w_out, w, 4 * P, cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return e;
@@ -1151,7 +1172,7 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
   if (e != cudaSuccess) return e;
   {
     ProfScope ps(prof, kKCombine, st);
-    k_combine_weighted<<<T, 256, 0, st>>>(T, residual, y, w, y + P * kHidden, coef, out);
+    k_combine_weighted<<<T, 256, 0, st>>>(T, residual, y, w, y + P * kHidden, coef, out, eps, x16_next);
   }
   return cudaGetLastError();
 }

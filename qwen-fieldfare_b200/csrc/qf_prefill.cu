@@ -510,21 +510,28 @@ __global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
 //
 // Warp roles: 0-7 weight producers (warp w: block w >> 2, TMEM lanes
 // 32 * (w & 3) ...), 8-15 epilogue, 16-17 MMA issue (one thread each; warp 16
-// also allocates TMEM), 18 loads (one thread issues the TMAs).
+// also allocates TMEM), 18 weight loads, 19 token loads (one thread each
+// issues the TMAs: the weight stream is gated only by the producers, the token
+// tiles only by the MMAs that free their stages).
 //
 // The weights reach shared memory by TMA too: per 64-column step one tiled
 // load brings the Q4 codes of the unit's 2 x 128 weight rows (32 bytes a row,
 // 8 KB) into a 6-stage ring, and per 8 steps one load each brings their
 // scales and biases (8 groups a row); producers read them from shared memory,
 // so the DRAM latency of the weights is covered by the ring, not by registers.
-constexpr int kGemmWarps = 19;
+constexpr int kGemmWarps = 20;
 constexpr int kGemmThreads = kGemmWarps * 32;
 constexpr int kMmaWarp = 16;
-constexpr int kLoadWarp = 18;
+constexpr int kLoadWarp = 18;  // weight codes, scales and biases
+constexpr int kTokWarp = 19;   // token tiles
 constexpr int kEpiThreads = 256;
 constexpr int kTokStages = 8;
 constexpr int kAStages = 4;           // TMEM A stages
 constexpr int kTokStageBytes = kTileRows * 128;  // 128 rows x 64 fp16, 128-byte swizzle
+// a tile of <= 16 rows (decode batches: 1-4 positions per expert) loads only
+// its 16 rows: the MMA of N = 16 reads no further, and the 128-byte swizzle
+// pattern repeats every 8 rows, so the stage layout is the same
+constexpr int kSmallTileRows = 16;
 constexpr int kCodeStages = 6;
 constexpr int kCodeStageBytes = 2 * 128 * 32;    // 2 blocks x 128 rows x 64 Q4 codes
 constexpr int kSbWin = 8;                        // steps per scale/bias window
@@ -556,6 +563,7 @@ static_assert(kGemmSmem > 114 * 1024, "one CTA per SM: the kernel allocates all 
 
 struct GemmArgs {
   CUtensorMap map_rows;  // B operand rows: MODE 0 gathered x [P+T][2048], MODE 1 act [P+T][512]; box 64 x 128
+  CUtensorMap map_rows_small;  // the same rows, box 64 x kSmallTileRows (tiles of <= 16 rows)
   // weights, [0] the bank, [1] the shared record: codes (box 32 bytes x 2 x 128
   // rows), scales and biases (box 8 groups x 2 x 128 rows)
   CUtensorMap map_code[2], map_s[2], map_b[2];
@@ -815,14 +823,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
         tc_commit(&sy->acc_full);
       }
     }
-  } else if (lane == 0) {
-    // ---------------- loads by TMA, per 64-column step: the unit's weight codes
-    // (and every 8 steps their scales and biases), then the token tile
+  } else if (warp == kLoadWarp && lane == 0) {
+    // ---------------- weight loads by TMA, per 64-column step: the unit's codes
+    // (and every 8 steps their scales and biases); gated only by the producers,
+    // so the weight stream runs as far ahead as the rings allow
     int gs = 0;
     for (int i = 0; i < my_units; i++) {
       const int u = blockIdx.x + i * G;
       const int4 t = a.tiles[u / PARTS];
-      const int pb = t.w + t.y;
       const int part = u % PARTS;
       const int src = t.x == kExperts ? 1 : 0;
       const int rec = src ? 0 : t.x;
@@ -846,10 +854,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
           tma_load4(codes + cs * kCodeStageBytes, &a.map_code[src], ks * 32, part * 128, 0, rec, &sy->code_full[cs]);
         else
           tma_load3(codes + cs * kCodeStageBytes, &a.map_code[src], ks * 32, part * 256, rec, &sy->code_full[cs]);
+      }
+    }
+  } else if (warp == kTokWarp && lane == 0) {
+    // ---------------- token tiles by TMA (gated by the MMAs that free the stages)
+    int gs = 0;
+    for (int i = 0; i < my_units; i++) {
+      const int u = blockIdx.x + i * G;
+      const int4 t = a.tiles[u / PARTS];
+      const int pb = t.w + t.y;
+      const bool small = t.z <= kSmallTileRows;
+      for (int ks = 0; ks < KS; ks++, gs++) {
         const int ts = gs % kTokStages;
         if (!mbar_wait(&sy->tok_empty[ts], ((gs / kTokStages) & 1) ^ 1)) ok = false;
-        mbar_expect_tx(&sy->tok_full[ts], kTokStageBytes);
-        tma_tile(ring + ts * kTokStageBytes, &a.map_rows, ks * 64, pb, &sy->tok_full[ts]);
+        mbar_expect_tx(&sy->tok_full[ts], small ? kSmallTileRows * 128 : kTokStageBytes);
+        tma_tile(ring + ts * kTokStageBytes, small ? &a.map_rows_small : &a.map_rows, ks * 64, pb, &sy->tok_full[ts]);
       }
     }
   }
@@ -1061,7 +1080,9 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
                         __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
                         size_t max_tiles, int sms, int* status, Prof* prof, const EpOut* ep) {
   GemmArgs g0, g1;
-  if (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows))
+  if (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows) ||
+      !encode_rows(&g0.map_rows_small, rows, R, kHidden, kSmallTileRows) ||
+      !encode_rows(&g1.map_rows_small, act, R, kInter, kSmallTileRows))
     return cudaErrorInvalidValue;
   if (!encode_weights(&g0, 0, 0, L.bank, L.bank_records, L.stride) ||
       !encode_weights(&g0, 1, 0, L.shared, 1, L.stride) ||

@@ -272,8 +272,10 @@ def main():
         return float(t.item())
 
     def measure(T: int, steps: int, warmup: int, profile: bool, e2e: bool = False):
-        # T <= 8 runs one persistent kernel per step (the whole stack); larger T
-        # runs five kernels per block, of which k_gate_up streams the most bytes
+        # T <= 8 runs one persistent kernel per step (the whole stack); T = 9..64
+        # (resident bank) runs the grouped path per block: router, plan (+ top-8
+        # up to 32 tokens, a separate top-k launch above), gather, the gate/up and
+        # down tcgen05 GEMMs, combine; the gate/up GEMM streams the most bytes
         prof_kernel = "fused" if T <= 8 else "gate_up"
         pool = torch.stack([Q.synth_hidden(1000 + rank, i * T, T) for i in range(POOL)])
         pool_dev = pool.to(dev)
@@ -354,11 +356,12 @@ def main():
                                + uniq[last].sum() * RECORD)
             else:
                 kbytes = float(np.mean((uniq[last] + 1) * GATE_UP_BYTES))
-            res["kernel"] = ("k_fused1" if T == 1 else "k_fused") if prof_kernel == "fused" else "k_gate_up"
+            res["kernel"] = (("k_fused1" if T == 1 else "k_fused") if prof_kernel == "fused"
+                             else "k_grouped<0> (gate/up)")
             res["kernel_ms"] = tot_ms / max(n, 1)
             res["kernel_launches"] = n
             res["kernel_bytes"] = kbytes
-            res["launches_per_step"] = 1 if prof_kernel == "fused" else 5 * args.layers
+            res["launches_per_step"] = 1 if prof_kernel == "fused" else (6 if T <= 32 else 7) * args.layers
         del g
         return res
 

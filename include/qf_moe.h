@@ -272,6 +272,71 @@ qf_status qf_tier_fetch(qf_tier *t, const int64_t *host_index, const uint32_t *s
 qf_status qf_tier_stats(const qf_tier *t, int64_t *copies, int64_t *bytes);
 qf_status qf_tier_synchronize(qf_tier *t);
 
+/* ---- packed expert store, format v2 (host) ----------------------------- */
+/* Reader of the reference's packed expert files, the source of the host
+ * tier: <directory>/manifest.json plus layer_00.q4exp .. layer_39.q4exp, each
+ * a 4,096-byte little-endian header followed by 256 records of 1,769,472
+ * bytes in expert order -- the slot layout above, byte for byte
+ * (Sources/QwenFieldfareCore/Storage/QwenQ4ExpertStore.swift:50-159, written
+ * by QwenQ4ExpertStoreBuilder.swift:284-352).  Failures return QF_ERR_ARG
+ * (invalid manifest, header or source index) or QF_ERR_IO (open, stat,
+ * short read); qf_store_last_error() gives the message on the calling
+ * thread.  The reader is thread-safe; counters are atomic. */
+#define QF_STORE_HEADER_BYTES 4096
+typedef struct qf_store_header {
+    int32_t layer_index;
+    int32_t experts_per_layer;
+    int32_t expert_byte_length;
+    uint64_t payload_byte_length;
+    char payload_sha256[65];        /* 64 lowercase hex characters + NUL */
+    char source_index_sha256[65];
+} qf_store_header;
+/* QwenQ4ExpertLayerHeader.encode (QwenQ4ExpertStore.swift:76-99): out gets
+ * QF_STORE_HEADER_BYTES bytes; rejects digests that are not 64 lowercase hex
+ * characters and negative or zero counts. */
+qf_status qf_store_header_encode(const qf_store_header *h, uint8_t *out);
+/* QwenQ4ExpertLayerHeader.decode (QwenQ4ExpertStore.swift:101-124): checks
+ * length, magic "Q4EXP02\0", schema 2, header length and both digests. */
+qf_status qf_store_header_decode(const uint8_t *bytes, size_t n, qf_store_header *out);
+/* QwenQ4ExpertStore.validateManifest (QwenQ4ExpertStore.swift:322-342) on the
+ * text of manifest.json: schema 2, a valid source digest, every layer 0..39
+ * exactly once with its canonical file name and size and a valid digest. */
+qf_status qf_store_validate_manifest(const char *json, size_t n);
+
+typedef struct qf_store qf_store;
+/* QwenQ4ExpertStore.init (QwenQ4ExpertStore.swift:213-282): validates the
+ * manifest, opens the 40 layer files (regular files, no symlink followed),
+ * checks each size and each header against the manifest.  With
+ * source_index_path (the checkpoint's model.safetensors.index.json) its
+ * SHA-256 must equal the manifest's; NULL skips that check. */
+qf_status qf_store_open(const char *directory, const char *source_index_path, qf_store **out);
+void qf_store_close(qf_store *s);
+/* QwenQ4ExpertStore.readExpert (QwenQ4ExpertStore.swift:288-306): one
+ * 1,769,472-byte record into dst (host memory). */
+qf_status qf_store_read_expert(qf_store *s, int32_t layer, int32_t expert, void *dst);
+/* Fills a host tier for qf_tier_create: record (layer - first_layer) * 256 +
+ * expert at host_records + index * host_record_stride, for layers
+ * [first_layer, first_layer + n_layers), read by `threads` threads (<= 0: 8).
+ * Replaces the per-miss pread of the streaming runner
+ * (QwenQ4ActiveExpertStreamingRunner.swift:839-888) with one load up front. */
+qf_status qf_store_load_tier(qf_store *s, int32_t first_layer, int32_t n_layers, void *host_records,
+                             uint64_t host_record_stride, int32_t threads);
+typedef struct qf_store_metrics {
+    int64_t packed_reads;       /* records read in full */
+    int64_t pread_operations;   /* record reads issued */
+    int64_t read_failures;      /* out-of-range requests and short reads */
+} qf_store_metrics;
+/* QwenQ4ExpertStore.metricsSnapshot (QwenQ4ExpertStore.swift:308-316),
+ * kind "qwen-q4-packed-v2". */
+qf_status qf_store_get_metrics(const qf_store *s, qf_store_metrics *out);
+/* SHA-256 of one layer's payload against the manifest digest (the builder's
+ * layer check, QwenQ4ExpertStoreBuilder.swift:354-370): *matches = 1 or 0. */
+qf_status qf_store_verify_layer(qf_store *s, int32_t layer, int32_t *matches);
+/* SHA-256 of n bytes as 64 lowercase hex characters + NUL (out: 65 bytes). */
+qf_status qf_sha256_hex(const void *data, size_t n, char *out);
+/* Message of the last failed qf_store_* / qf_sha256_hex call on this thread. */
+const char *qf_store_last_error(void);
+
 /* One batch-1 decode step through n_layers MoE blocks whose routed experts
  * stream through the cache: the active-streaming forwardToken MoE loop
  * (QwenQ4ActiveExpertStreamingRunner.swift:958-1381 with

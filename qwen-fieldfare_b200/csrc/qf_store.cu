@@ -1,0 +1,716 @@
+// Packed expert store, format v2: the reference's per-layer expert files,
+// read into the pinned-host tier (host code only).
+//
+// Format (Sources/QwenFieldfareCore/Storage/QwenQ4ExpertStore.swift:50-159,
+// written by QwenQ4ExpertStoreBuilder.swift:284-352):
+//   <dir>/manifest.json       {"schemaVersion": 2, "sourceIndexSHA256": hex,
+//                              "layers": [{"layerIndex", "filename",
+//                              "fileSize", "payloadSHA256"} x 40]}
+//   <dir>/layer_NN.q4exp      4,096-byte header, then 256 expert records of
+//                              1,769,472 bytes in expert order (the slot
+//                              layout of the HBM arena, byte for byte)
+// Header, little-endian: magic "Q4EXP02\0" [0,8), u32 schema 2 @8, u32
+// header length 4096 @12, u32 layer @16, u32 experts per layer @20, u32
+// record bytes @24, u64 payload bytes @32, payload SHA-256 as 64 lowercase
+// hex characters [40,104), source-index SHA-256 [104,168), zeros after.
+// The payload digest is the SHA-256 of the 256 records.
+
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cerrno>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/qf_moe.h"
+
+namespace {
+
+constexpr int kLayers = 40;
+constexpr int kExpertsPerLayer = 256;
+constexpr uint64_t kRecordBytes = 1769472;
+constexpr uint64_t kHeaderBytes = QF_STORE_HEADER_BYTES;
+constexpr uint64_t kPayloadBytes = kExpertsPerLayer * kRecordBytes;
+constexpr uint64_t kLayerFileBytes = kHeaderBytes + kPayloadBytes;
+constexpr uint32_t kSchema = 2;
+const uint8_t kMagic[8] = {'Q', '4', 'E', 'X', 'P', '0', '2', 0};
+
+thread_local std::string g_err;
+
+qf_status fail(qf_status s, const std::string& msg) {
+  g_err = msg;
+  return s;
+}
+
+// ---------------------------------------------------------------- SHA-256
+// FIPS 180-4, section 6.2: 64-byte blocks, big-endian words, 64 rounds.
+class Sha256 {
+ public:
+  Sha256() { reset(); }
+  void reset() {
+    static const uint32_t h0[8] = {0x6a09e667u, 0xbb67ae85u, 0x3c6ef372u, 0xa54ff53au,
+                                   0x510e527fu, 0x9b05688cu, 0x1f83d9abu, 0x5be0cd19u};
+    std::memcpy(h_, h0, sizeof(h_));
+    len_ = 0;
+    fill_ = 0;
+  }
+  void update(const void* data, size_t n) {
+    const uint8_t* p = static_cast<const uint8_t*>(data);
+    len_ += n;
+    if (fill_) {
+      const size_t take = std::min(n, sizeof(buf_) - fill_);
+      std::memcpy(buf_ + fill_, p, take);
+      fill_ += take;
+      p += take;
+      n -= take;
+      if (fill_ < sizeof(buf_)) return;
+      block(buf_);
+      fill_ = 0;
+    }
+    for (; n >= 64; p += 64, n -= 64) block(p);
+    std::memcpy(buf_, p, n);
+    fill_ = n;
+  }
+  std::string hex() {
+    const uint64_t bits = len_ * 8;
+    const uint8_t pad0 = 0x80, zero = 0;
+    update(&pad0, 1);
+    while (fill_ != 56) update(&zero, 1);
+    uint8_t lenbe[8];
+    for (int i = 0; i < 8; i++) lenbe[i] = static_cast<uint8_t>(bits >> (56 - 8 * i));
+    update(lenbe, 8);
+    static const char* digits = "0123456789abcdef";
+    std::string out(64, '0');
+    for (int i = 0; i < 8; i++)
+      for (int b = 0; b < 4; b++) {
+        const uint8_t v = static_cast<uint8_t>(h_[i] >> (24 - 8 * b));
+        out[i * 8 + b * 2] = digits[v >> 4];
+        out[i * 8 + b * 2 + 1] = digits[v & 15];
+      }
+    return out;
+  }
+
+ private:
+  static uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+  void block(const uint8_t* p) {
+    static const uint32_t k[64] = {
+        0x428a2f98u, 0x71374491u, 0xb5c0fbcfu, 0xe9b5dba5u, 0x3956c25bu, 0x59f111f1u, 0x923f82a4u, 0xab1c5ed5u,
+        0xd807aa98u, 0x12835b01u, 0x243185beu, 0x550c7dc3u, 0x72be5d74u, 0x80deb1feu, 0x9bdc06a7u, 0xc19bf174u,
+        0xe49b69c1u, 0xefbe4786u, 0x0fc19dc6u, 0x240ca1ccu, 0x2de92c6fu, 0x4a7484aau, 0x5cb0a9dcu, 0x76f988dau,
+        0x983e5152u, 0xa831c66du, 0xb00327c8u, 0xbf597fc7u, 0xc6e00bf3u, 0xd5a79147u, 0x06ca6351u, 0x14292967u,
+        0x27b70a85u, 0x2e1b2138u, 0x4d2c6dfcu, 0x53380d13u, 0x650a7354u, 0x766a0abbu, 0x81c2c92eu, 0x92722c85u,
+        0xa2bfe8a1u, 0xa81a664bu, 0xc24b8b70u, 0xc76c51a3u, 0xd192e819u, 0xd6990624u, 0xf40e3585u, 0x106aa070u,
+        0x19a4c116u, 0x1e376c08u, 0x2748774cu, 0x34b0bcb5u, 0x391c0cb3u, 0x4ed8aa4au, 0x5b9cca4fu, 0x682e6ff3u,
+        0x748f82eeu, 0x78a5636fu, 0x84c87814u, 0x8cc70208u, 0x90befffau, 0xa4506cebu, 0xbef9a3f7u, 0xc67178f2u};
+    uint32_t w[64];
+    for (int i = 0; i < 16; i++)
+      w[i] = (uint32_t)p[4 * i] << 24 | (uint32_t)p[4 * i + 1] << 16 | (uint32_t)p[4 * i + 2] << 8 | p[4 * i + 3];
+    for (int i = 16; i < 64; i++) {
+      const uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
+      const uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
+      w[i] = w[i - 16] + s0 + w[i - 7] + s1;
+    }
+    uint32_t a = h_[0], b = h_[1], c = h_[2], d = h_[3], e = h_[4], f = h_[5], g = h_[6], h = h_[7];
+    for (int i = 0; i < 64; i++) {
+      const uint32_t t1 = h + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + k[i] + w[i];
+      const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
+      h = g;
+      g = f;
+      f = e;
+      e = d + t1;
+      d = c;
+      c = b;
+      b = a;
+      a = t1 + t2;
+    }
+    h_[0] += a;
+    h_[1] += b;
+    h_[2] += c;
+    h_[3] += d;
+    h_[4] += e;
+    h_[5] += f;
+    h_[6] += g;
+    h_[7] += h;
+  }
+  uint32_t h_[8];
+  uint64_t len_;
+  uint8_t buf_[64];
+  size_t fill_;
+};
+
+bool is_sha256(const char* s, size_t n) {
+  if (n != 64) return false;
+  for (size_t i = 0; i < n; i++)
+    if (!((s[i] >= '0' && s[i] <= '9') || (s[i] >= 'a' && s[i] <= 'f'))) return false;
+  return true;
+}
+bool is_sha256(const std::string& s) { return is_sha256(s.data(), s.size()); }
+
+// ---------------------------------------------------------------- JSON
+// Just enough JSON for the manifest: objects, arrays, strings, numbers,
+// literals; numbers keep their integral value when they have one.
+struct Json {
+  enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
+  bool b = false;
+  double num = 0;
+  bool integral = false;
+  int64_t i = 0;
+  std::string s;
+  std::vector<Json> arr;
+  std::map<std::string, Json> obj;
+};
+
+class JsonParser {
+ public:
+  JsonParser(const char* p, size_t n) : p_(p), end_(p + n) {}
+  bool parse(Json& out) {
+    if (!value(out, 0)) return false;
+    ws();
+    return p_ == end_;
+  }
+
+ private:
+  void ws() {
+    while (p_ < end_ && (*p_ == ' ' || *p_ == '\t' || *p_ == '\n' || *p_ == '\r')) p_++;
+  }
+  bool lit(const char* w) {
+    const size_t n = std::strlen(w);
+    if ((size_t)(end_ - p_) < n || std::strncmp(p_, w, n) != 0) return false;
+    p_ += n;
+    return true;
+  }
+  static void utf8(std::string& o, uint32_t c) {
+    if (c < 0x80) {
+      o += (char)c;
+    } else if (c < 0x800) {
+      o += (char)(0xC0 | (c >> 6));
+      o += (char)(0x80 | (c & 0x3F));
+    } else if (c < 0x10000) {
+      o += (char)(0xE0 | (c >> 12));
+      o += (char)(0x80 | ((c >> 6) & 0x3F));
+      o += (char)(0x80 | (c & 0x3F));
+    } else {
+      o += (char)(0xF0 | (c >> 18));
+      o += (char)(0x80 | ((c >> 12) & 0x3F));
+      o += (char)(0x80 | ((c >> 6) & 0x3F));
+      o += (char)(0x80 | (c & 0x3F));
+    }
+  }
+  bool hex4(uint32_t& v) {
+    if (end_ - p_ < 4) return false;
+    v = 0;
+    for (int k = 0; k < 4; k++) {
+      const char c = *p_++;
+      v <<= 4;
+      if (c >= '0' && c <= '9') v |= (uint32_t)(c - '0');
+      else if (c >= 'a' && c <= 'f') v |= (uint32_t)(c - 'a' + 10);
+      else if (c >= 'A' && c <= 'F') v |= (uint32_t)(c - 'A' + 10);
+      else return false;
+    }
+    return true;
+  }
+  bool str(std::string& o) {
+    if (p_ >= end_ || *p_ != '"') return false;
+    p_++;
+    while (p_ < end_ && *p_ != '"') {
+      char c = *p_++;
+      if ((unsigned char)c < 0x20) return false;
+      if (c != '\\') {
+        o += c;
+        continue;
+      }
+      if (p_ >= end_) return false;
+      c = *p_++;
+      switch (c) {
+        case '"': o += '"'; break;
+        case '\\': o += '\\'; break;
+        case '/': o += '/'; break;
+        case 'b': o += '\b'; break;
+        case 'f': o += '\f'; break;
+        case 'n': o += '\n'; break;
+        case 'r': o += '\r'; break;
+        case 't': o += '\t'; break;
+        case 'u': {
+          uint32_t v;
+          if (!hex4(v)) return false;
+          if (v >= 0xD800 && v < 0xDC00) {
+            uint32_t lo;
+            if (end_ - p_ < 2 || p_[0] != '\\' || p_[1] != 'u') return false;
+            p_ += 2;
+            if (!hex4(lo) || lo < 0xDC00 || lo >= 0xE000) return false;
+            v = 0x10000 + ((v - 0xD800) << 10) + (lo - 0xDC00);
+          }
+          utf8(o, v);
+          break;
+        }
+        default: return false;
+      }
+    }
+    if (p_ >= end_) return false;
+    p_++;
+    return true;
+  }
+  bool number(Json& o) {
+    const char* s = p_;
+    if (p_ < end_ && *p_ == '-') p_++;
+    if (p_ >= end_ || !(*p_ >= '0' && *p_ <= '9')) return false;
+    if (*p_ == '0') p_++;
+    else while (p_ < end_ && *p_ >= '0' && *p_ <= '9') p_++;
+    bool plain = true;
+    if (p_ < end_ && *p_ == '.') {
+      plain = false;
+      p_++;
+      if (p_ >= end_ || !(*p_ >= '0' && *p_ <= '9')) return false;
+      while (p_ < end_ && *p_ >= '0' && *p_ <= '9') p_++;
+    }
+    if (p_ < end_ && (*p_ == 'e' || *p_ == 'E')) {
+      plain = false;
+      p_++;
+      if (p_ < end_ && (*p_ == '+' || *p_ == '-')) p_++;
+      if (p_ >= end_ || !(*p_ >= '0' && *p_ <= '9')) return false;
+      while (p_ < end_ && *p_ >= '0' && *p_ <= '9') p_++;
+    }
+    const std::string text(s, p_);
+    o.kind = Json::Num;
+    o.num = std::strtod(text.c_str(), nullptr);
+    if (plain && text.size() <= 18) {
+      o.integral = true;
+      o.i = std::strtoll(text.c_str(), nullptr, 10);
+    } else if (o.num == (double)(int64_t)o.num && std::abs(o.num) < 9.0e15) {
+      o.integral = true;
+      o.i = (int64_t)o.num;
+    }
+    return true;
+  }
+  bool value(Json& o, int depth) {
+    if (depth > 16) return false;
+    ws();
+    if (p_ >= end_) return false;
+    const char c = *p_;
+    if (c == '{') {
+      p_++;
+      o.kind = Json::Obj;
+      ws();
+      if (p_ < end_ && *p_ == '}') {
+        p_++;
+        return true;
+      }
+      for (;;) {
+        ws();
+        std::string key;
+        if (!str(key)) return false;
+        ws();
+        if (p_ >= end_ || *p_ != ':') return false;
+        p_++;
+        Json v;
+        if (!value(v, depth + 1)) return false;
+        o.obj[key] = std::move(v);
+        ws();
+        if (p_ < end_ && *p_ == ',') {
+          p_++;
+          continue;
+        }
+        if (p_ < end_ && *p_ == '}') {
+          p_++;
+          return true;
+        }
+        return false;
+      }
+    }
+    if (c == '[') {
+      p_++;
+      o.kind = Json::Arr;
+      ws();
+      if (p_ < end_ && *p_ == ']') {
+        p_++;
+        return true;
+      }
+      for (;;) {
+        Json v;
+        if (!value(v, depth + 1)) return false;
+        o.arr.push_back(std::move(v));
+        ws();
+        if (p_ < end_ && *p_ == ',') {
+          p_++;
+          continue;
+        }
+        if (p_ < end_ && *p_ == ']') {
+          p_++;
+          return true;
+        }
+        return false;
+      }
+    }
+    if (c == '"') {
+      o.kind = Json::Str;
+      return str(o.s);
+    }
+    if (lit("true")) {
+      o.kind = Json::Bool;
+      o.b = true;
+      return true;
+    }
+    if (lit("false")) {
+      o.kind = Json::Bool;
+      return true;
+    }
+    if (lit("null")) return true;
+    return number(o);
+  }
+  const char* p_;
+  const char* end_;
+};
+
+// ---------------------------------------------------------------- manifest
+struct LayerEntry {
+  int64_t layer_index = -1;
+  std::string filename;
+  int64_t file_size = 0;
+  std::string payload_sha256;
+};
+struct Manifest {
+  int64_t schema_version = 0;
+  std::string source_index_sha256;
+  std::vector<LayerEntry> layers;  // sorted by layer index once validated
+};
+
+std::string layer_filename(int layer) {
+  char b[32];
+  std::snprintf(b, sizeof b, "layer_%02d.q4exp", layer);
+  return b;
+}
+
+bool get_int(const Json& o, const char* key, int64_t& v) {
+  auto it = o.obj.find(key);
+  if (it == o.obj.end() || it->second.kind != Json::Num || !it->second.integral) return false;
+  v = it->second.i;
+  return true;
+}
+bool get_str(const Json& o, const char* key, std::string& v) {
+  auto it = o.obj.find(key);
+  if (it == o.obj.end() || it->second.kind != Json::Str) return false;
+  v = it->second.s;
+  return true;
+}
+
+// JSONDecoder of QwenQ4ExpertStoreManifest (QwenQ4ExpertStore.swift:24-48),
+// then QwenQ4ExpertStore.validateManifest (:322-342)
+qf_status parse_manifest(const char* text, size_t n, Manifest& m) {
+  Json root;
+  if (!JsonParser(text, n).parse(root) || root.kind != Json::Obj)
+    return fail(QF_ERR_ARG, "invalid manifest: not a JSON object");
+  auto lay = root.obj.find("layers");
+  if (!get_int(root, "schemaVersion", m.schema_version) ||
+      !get_str(root, "sourceIndexSHA256", m.source_index_sha256) || lay == root.obj.end() ||
+      lay->second.kind != Json::Arr)
+    return fail(QF_ERR_ARG, "invalid manifest: missing or mistyped schemaVersion / sourceIndexSHA256 / layers");
+  for (const Json& e : lay->second.arr) {
+    LayerEntry le;
+    if (e.kind != Json::Obj || !get_int(e, "layerIndex", le.layer_index) || !get_str(e, "filename", le.filename) ||
+        !get_int(e, "fileSize", le.file_size) || !get_str(e, "payloadSHA256", le.payload_sha256))
+      return fail(QF_ERR_ARG, "invalid manifest: malformed layer entry");
+    m.layers.push_back(le);
+  }
+  if (m.schema_version != (int64_t)kSchema)
+    return fail(QF_ERR_ARG, "invalid manifest: unsupported schema version " + std::to_string(m.schema_version));
+  if (!is_sha256(m.source_index_sha256)) return fail(QF_ERR_ARG, "invalid manifest: invalid source index SHA-256");
+  if ((int)m.layers.size() != kLayers)
+    return fail(QF_ERR_ARG, "invalid manifest: expected 40 layers, got " + std::to_string(m.layers.size()));
+  std::stable_sort(m.layers.begin(), m.layers.end(),
+                   [](const LayerEntry& a, const LayerEntry& b) { return a.layer_index < b.layer_index; });
+  for (int i = 0; i < kLayers; i++) {
+    const LayerEntry& le = m.layers[i];
+    if (le.layer_index != i || le.filename != layer_filename(i) || le.file_size != (int64_t)kLayerFileBytes ||
+        !is_sha256(le.payload_sha256))
+      return fail(QF_ERR_ARG, "invalid manifest: invalid layer entry " + std::to_string(i));
+  }
+  return QF_OK;
+}
+
+// ---------------------------------------------------------------- files
+void put32(uint8_t* b, uint32_t v) {
+  for (int i = 0; i < 4; i++) b[i] = (uint8_t)(v >> (8 * i));
+}
+void put64(uint8_t* b, uint64_t v) {
+  for (int i = 0; i < 8; i++) b[i] = (uint8_t)(v >> (8 * i));
+}
+uint32_t get32(const uint8_t* b) {
+  uint32_t v = 0;
+  for (int i = 0; i < 4; i++) v |= (uint32_t)b[i] << (8 * i);
+  return v;
+}
+uint64_t get64(const uint8_t* b) {
+  uint64_t v = 0;
+  for (int i = 0; i < 8; i++) v |= (uint64_t)b[i] << (8 * i);
+  return v;
+}
+
+// QwenQ4ExpertStore.preadFully (:344-364): retries on EINTR, stops at EOF
+size_t pread_fully(int fd, void* dst, size_t count, uint64_t offset) {
+  size_t done = 0;
+  while (done < count) {
+    const ssize_t r = ::pread(fd, static_cast<uint8_t*>(dst) + done, count - done, (off_t)(offset + done));
+    if (r < 0 && errno == EINTR) continue;
+    if (r <= 0) return done;
+    done += (size_t)r;
+  }
+  return done;
+}
+
+bool read_file(const std::string& path, std::string& out) {
+  const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return false;
+  char buf[1 << 16];
+  for (;;) {
+    const ssize_t r = ::read(fd, buf, sizeof buf);
+    if (r < 0 && errno == EINTR) continue;
+    if (r < 0) {
+      ::close(fd);
+      return false;
+    }
+    if (r == 0) break;
+    out.append(buf, (size_t)r);
+  }
+  ::close(fd);
+  return true;
+}
+
+bool hash_file(const std::string& path, std::string& hex) {
+  const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return false;
+  Sha256 h;
+  std::vector<uint8_t> buf(1 << 20);
+  uint64_t off = 0;
+  for (;;) {
+    const size_t got = pread_fully(fd, buf.data(), buf.size(), off);
+    h.update(buf.data(), got);
+    off += got;
+    if (got < buf.size()) break;
+  }
+  ::close(fd);
+  hex = h.hex();
+  return true;
+}
+
+}  // namespace
+
+struct qf_store {
+  std::string dir;
+  Manifest manifest;
+  int fds[kLayers];
+  std::atomic<int64_t> packed_reads{0};
+  std::atomic<int64_t> pread_ops{0};
+  std::atomic<int64_t> failures{0};
+  qf_store() {
+    for (int& f : fds) f = -1;
+  }
+  ~qf_store() {
+    for (int f : fds)
+      if (f >= 0) ::close(f);
+  }
+  bool read_expert(int layer, int expert, void* dst) {
+    if (layer < 0 || layer >= kLayers || expert < 0 || expert >= kExpertsPerLayer || !dst) {
+      failures++;
+      return false;
+    }
+    const size_t got = pread_fully(fds[layer], dst, kRecordBytes, kHeaderBytes + (uint64_t)expert * kRecordBytes);
+    pread_ops++;
+    if (got != kRecordBytes) {
+      failures++;
+      return false;
+    }
+    packed_reads++;
+    return true;
+  }
+};
+
+extern "C" {
+
+qf_status qf_sha256_hex(const void* data, size_t n, char* out) {
+  if ((!data && n) || !out) return fail(QF_ERR_ARG, "qf_sha256_hex: null pointer");
+  Sha256 h;
+  h.update(data, n);
+  const std::string hex = h.hex();
+  std::memcpy(out, hex.c_str(), 65);
+  return QF_OK;
+}
+
+qf_status qf_store_header_encode(const qf_store_header* h, uint8_t* out) {
+  if (!h || !out) return fail(QF_ERR_ARG, "invalid header: null pointer");
+  const size_t lp = strnlen(h->payload_sha256, sizeof h->payload_sha256);
+  const size_t ls = strnlen(h->source_index_sha256, sizeof h->source_index_sha256);
+  if (!is_sha256(h->payload_sha256, lp) || !is_sha256(h->source_index_sha256, ls))
+    return fail(QF_ERR_ARG, "invalid header: SHA-256 fields must be 64 lowercase hexadecimal characters");
+  if (h->layer_index < 0 || h->experts_per_layer <= 0 || h->expert_byte_length <= 0)
+    return fail(QF_ERR_ARG, "invalid header: numeric field is out of range");
+  std::memset(out, 0, kHeaderBytes);
+  std::memcpy(out, kMagic, 8);
+  put32(out + 8, kSchema);
+  put32(out + 12, (uint32_t)kHeaderBytes);
+  put32(out + 16, (uint32_t)h->layer_index);
+  put32(out + 20, (uint32_t)h->experts_per_layer);
+  put32(out + 24, (uint32_t)h->expert_byte_length);
+  put64(out + 32, h->payload_byte_length);
+  std::memcpy(out + 40, h->payload_sha256, 64);
+  std::memcpy(out + 104, h->source_index_sha256, 64);
+  return QF_OK;
+}
+
+qf_status qf_store_header_decode(const uint8_t* b, size_t n, qf_store_header* out) {
+  if (!b || !out) return fail(QF_ERR_ARG, "invalid header: null pointer");
+  if (n != kHeaderBytes)
+    return fail(QF_ERR_ARG, "invalid header: expected 4096 bytes, got " + std::to_string(n));
+  if (std::memcmp(b, kMagic, 8) != 0) return fail(QF_ERR_ARG, "invalid header: magic mismatch");
+  if (get32(b + 8) != kSchema) return fail(QF_ERR_ARG, "invalid header: unsupported schema version");
+  if (get32(b + 12) != (uint32_t)kHeaderBytes) return fail(QF_ERR_ARG, "invalid header: header byte length mismatch");
+  if (!is_sha256(reinterpret_cast<const char*>(b + 40), 64) ||
+      !is_sha256(reinterpret_cast<const char*>(b + 104), 64))
+    return fail(QF_ERR_ARG, "invalid header: invalid SHA-256 field");
+  const uint32_t layer = get32(b + 16), experts = get32(b + 20), bytes = get32(b + 24);
+  if (layer > 0x7fffffffu || experts > 0x7fffffffu || bytes > 0x7fffffffu)
+    return fail(QF_ERR_ARG, "invalid header: numeric field is out of range");
+  qf_store_header h;
+  std::memset(&h, 0, sizeof h);
+  h.layer_index = (int32_t)layer;
+  h.experts_per_layer = (int32_t)experts;
+  h.expert_byte_length = (int32_t)bytes;
+  h.payload_byte_length = get64(b + 32);
+  std::memcpy(h.payload_sha256, b + 40, 64);
+  std::memcpy(h.source_index_sha256, b + 104, 64);
+  *out = h;
+  return QF_OK;
+}
+
+qf_status qf_store_validate_manifest(const char* json, size_t n) {
+  if (!json) return fail(QF_ERR_ARG, "invalid manifest: null pointer");
+  Manifest m;
+  return parse_manifest(json, n, m);
+}
+
+qf_status qf_store_open(const char* directory, const char* source_index_path, qf_store** out) {
+  if (!directory || !out) return fail(QF_ERR_ARG, "qf_store_open: null pointer");
+  *out = nullptr;
+  std::unique_ptr<qf_store> s(new qf_store);
+  s->dir = directory;
+  const std::string mpath = s->dir + "/manifest.json";
+  std::string text;
+  if (!read_file(mpath, text)) return fail(QF_ERR_IO, "open failed for " + mpath + ": errno " + std::to_string(errno));
+  qf_status st = parse_manifest(text.data(), text.size(), s->manifest);
+  if (st != QF_OK) return st;
+  if (source_index_path) {
+    std::string actual;
+    if (!hash_file(source_index_path, actual))
+      return fail(QF_ERR_IO, std::string("open failed for ") + source_index_path);
+    if (actual != s->manifest.source_index_sha256)
+      return fail(QF_ERR_ARG, "source mismatch: the store belongs to a different source index (expected " +
+                                  s->manifest.source_index_sha256 + ", got " + actual + ")");
+  }
+  for (int l = 0; l < kLayers; l++) {
+    const LayerEntry& le = s->manifest.layers[l];
+    const std::string path = s->dir + "/" + le.filename;
+    const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC | O_NOFOLLOW);
+    if (fd < 0) return fail(QF_ERR_IO, "open failed for " + path + ": errno " + std::to_string(errno));
+    s->fds[l] = fd;
+    struct stat info;
+    if (::fstat(fd, &info) != 0 || !S_ISREG(info.st_mode))
+      return fail(QF_ERR_IO, "fstat failed for " + path + ": not a regular file");
+    if ((uint64_t)info.st_size != (uint64_t)le.file_size || (uint64_t)le.file_size != kLayerFileBytes)
+      return fail(QF_ERR_ARG, "invalid manifest: unexpected size for " + le.filename);
+    uint8_t hb[kHeaderBytes];
+    const size_t got = pread_fully(fd, hb, kHeaderBytes, 0);
+    if (got != kHeaderBytes)
+      return fail(QF_ERR_IO, "short read from " + path + ": expected 4096 bytes, got " + std::to_string(got));
+    qf_store_header h;
+    st = qf_store_header_decode(hb, kHeaderBytes, &h);
+    if (st != QF_OK) return st;
+    if (h.layer_index != le.layer_index || h.experts_per_layer != kExpertsPerLayer ||
+        (uint64_t)h.expert_byte_length != kRecordBytes || h.payload_byte_length != kPayloadBytes ||
+        le.payload_sha256 != std::string(h.payload_sha256, 64) ||
+        s->manifest.source_index_sha256 != std::string(h.source_index_sha256, 64))
+      return fail(QF_ERR_ARG, "invalid header: metadata mismatch in " + le.filename);
+  }
+  *out = s.release();
+  return QF_OK;
+}
+
+void qf_store_close(qf_store* s) { delete s; }
+
+qf_status qf_store_read_expert(qf_store* s, int32_t layer, int32_t expert, void* dst) {
+  if (!s) return fail(QF_ERR_ARG, "qf_store_read_expert: null store");
+  if (!s->read_expert(layer, expert, dst))
+    return fail(layer < 0 || layer >= kLayers || expert < 0 || expert >= kExpertsPerLayer || !dst ? QF_ERR_ARG
+                                                                                                 : QF_ERR_IO,
+                "read of layer " + std::to_string(layer) + " expert " + std::to_string(expert) + " failed");
+  return QF_OK;
+}
+
+qf_status qf_store_load_tier(qf_store* s, int32_t first_layer, int32_t n_layers, void* host_records,
+                             uint64_t host_record_stride, int32_t threads) {
+  if (!s || !host_records) return fail(QF_ERR_ARG, "qf_store_load_tier: null pointer");
+  if (first_layer < 0 || n_layers < 1 || first_layer + n_layers > kLayers || host_record_stride < kRecordBytes)
+    return fail(QF_ERR_ARG, "qf_store_load_tier: layers out of range or stride below one record");
+  const int64_t total = (int64_t)n_layers * kExpertsPerLayer;
+  const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 8, (int)std::min<int64_t>(total, 64)));
+  std::atomic<int64_t> next{0};
+  std::atomic<int64_t> bad{-1};
+  auto work = [&]() {
+    for (;;) {
+      const int64_t i = next.fetch_add(1);
+      if (i >= total) return;
+      uint8_t* dst = static_cast<uint8_t*>(host_records) + (uint64_t)i * host_record_stride;
+      if (!s->read_expert(first_layer + (int)(i / kExpertsPerLayer), (int)(i % kExpertsPerLayer), dst)) {
+        int64_t expect = -1;
+        bad.compare_exchange_strong(expect, i);
+      }
+    }
+  };
+  std::vector<std::thread> pool;
+  for (int t = 1; t < nt; t++) pool.emplace_back(work);
+  work();
+  for (auto& t : pool) t.join();
+  if (bad.load() >= 0) {
+    const int64_t i = bad.load();
+    return fail(QF_ERR_IO, "short read of layer " + std::to_string(first_layer + i / kExpertsPerLayer) +
+                               " expert " + std::to_string(i % kExpertsPerLayer));
+  }
+  return QF_OK;
+}
+
+qf_status qf_store_get_metrics(const qf_store* s, qf_store_metrics* out) {
+  if (!s || !out) return fail(QF_ERR_ARG, "qf_store_get_metrics: null pointer");
+  out->packed_reads = s->packed_reads.load();
+  out->pread_operations = s->pread_ops.load();
+  out->read_failures = s->failures.load();
+  return QF_OK;
+}
+
+qf_status qf_store_verify_layer(qf_store* s, int32_t layer, int32_t* matches) {
+  if (!s || !matches) return fail(QF_ERR_ARG, "qf_store_verify_layer: null pointer");
+  if (layer < 0 || layer >= kLayers) return fail(QF_ERR_ARG, "qf_store_verify_layer: layer out of range");
+  Sha256 h;
+  std::vector<uint8_t> buf(8u << 20);
+  uint64_t off = kHeaderBytes, left = kPayloadBytes;
+  while (left) {
+    const size_t want = (size_t)std::min<uint64_t>(left, buf.size());
+    const size_t got = pread_fully(s->fds[layer], buf.data(), want, off);
+    if (got != want) return fail(QF_ERR_IO, "short read while hashing layer " + std::to_string(layer));
+    h.update(buf.data(), got);
+    off += got;
+    left -= got;
+  }
+  *matches = h.hex() == s->manifest.layers[layer].payload_sha256 ? 1 : 0;
+  return QF_OK;
+}
+
+const char* qf_store_last_error(void) { return g_err.c_str(); }
+
+}  // extern "C"

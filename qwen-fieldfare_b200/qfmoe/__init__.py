@@ -6,6 +6,7 @@ hand-written sm_100a CUDA; there is no CPU fallback.
 from ._lib import QfError, lib  # noqa: F401
 from .cache import ArenaLayer, ExpertCache, HostTier, plan_slots, stream_step  # noqa: F401
 from .ep import ExpertParallel, exchange_handles  # noqa: F401
+from .store import ExpertStore  # noqa: F401
 from .moe import (  # noqa: F401
     DECODE_MAX_TOKENS, EXPERTS, HIDDEN, INTER, OFF, RECORD_BYTES, SHARED_EXPERT, TOPK,
     MoEContext, MoELayerWeights, StackPlan, block_forward, dispatch_plan, router_logits,

@@ -51,6 +51,17 @@ class CacheMetrics(C.Structure):
         "wasted_prefetches")]
 
 
+class StoreHeader(C.Structure):
+    _fields_ = [("layer_index", C.c_int32), ("experts_per_layer", C.c_int32),
+                ("expert_byte_length", C.c_int32), ("payload_byte_length", C.c_uint64),
+                ("payload_sha256", C.c_char * 65), ("source_index_sha256", C.c_char * 65)]
+
+
+class StoreMetrics(C.Structure):
+    _fields_ = [("packed_reads", C.c_int64), ("pread_operations", C.c_int64),
+                ("read_failures", C.c_int64)]
+
+
 # (name, restype, argtypes) for every symbol include/qf_moe.h declares.
 _P = C.c_void_p
 _I = C.c_int32
@@ -106,6 +117,17 @@ SIGNATURES = {
     "qf_synth_router": (_S, [_P, C.c_uint64, C.c_uint32, _P, _P, _P]),
     "qf_synth_coef": (_S, [_P, C.c_uint64, C.c_uint32, _P, _P, _P]),
     "qf_synth_hidden_host": (None, [C.c_uint64, C.c_uint64, _I, _P]),
+    "qf_store_header_encode": (_S, [C.POINTER(StoreHeader), _P]),
+    "qf_store_header_decode": (_S, [_P, C.c_size_t, C.POINTER(StoreHeader)]),
+    "qf_store_validate_manifest": (_S, [C.c_char_p, C.c_size_t]),
+    "qf_store_open": (_S, [C.c_char_p, C.c_char_p, C.POINTER(_P)]),
+    "qf_store_close": (None, [_P]),
+    "qf_store_read_expert": (_S, [_P, _I, _I, _P]),
+    "qf_store_load_tier": (_S, [_P, _I, _I, _P, C.c_uint64, _I]),
+    "qf_store_get_metrics": (_S, [_P, C.POINTER(StoreMetrics)]),
+    "qf_store_verify_layer": (_S, [_P, _I, C.POINTER(_I)]),
+    "qf_sha256_hex": (_S, [_P, C.c_size_t, _P]),
+    "qf_store_last_error": (C.c_char_p, []),
 }
 
 _lib = None

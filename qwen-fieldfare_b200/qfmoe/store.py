@@ -1,0 +1,137 @@
+"""Packed expert store (format v2): the reference's per-layer expert files as
+the source of the pinned-host tier (include/qf_moe.h, qf_store_*).
+
+The store directory holds manifest.json and layer_00.q4exp .. layer_39.q4exp;
+each layer file is a 4,096-byte header and 256 records of 1,769,472 bytes in
+expert order -- the HBM slot layout, so records go to the tier unchanged
+(Sources/QwenFieldfareCore/Storage/QwenQ4ExpertStore.swift:50-316).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from ._lib import QF_OK, QfError, StoreHeader, StoreMetrics, lib
+from .moe import EXPERTS, RECORD_BYTES
+
+HEADER_BYTES = 4096
+LAYERS = 40
+PAYLOAD_BYTES = EXPERTS * RECORD_BYTES
+LAYER_FILE_BYTES = HEADER_BYTES + PAYLOAD_BYTES
+
+
+def _ok(status: int) -> None:
+    if status != QF_OK:
+        raise QfError(status, lib().qf_store_last_error().decode())
+
+
+def layer_filename(layer: int) -> str:
+    """QwenQ4ExpertStore.layerFilename (QwenQ4ExpertStore.swift:200-202)."""
+    return f"layer_{layer:02d}.q4exp"
+
+
+def sha256_hex(data) -> str:
+    """SHA-256 (FIPS 180-4) of a bytes-like object, by the library."""
+    buf = np.frombuffer(memoryview(data), dtype=np.uint8)
+    out = C.create_string_buffer(65)
+    _ok(lib().qf_sha256_hex(C.c_void_p(buf.ctypes.data), buf.size, out))
+    return out.value.decode()
+
+
+def encode_header(layer_index: int, payload_sha256: str, source_index_sha256: str,
+                  experts_per_layer: int = EXPERTS, expert_byte_length: int = RECORD_BYTES,
+                  payload_byte_length: int = PAYLOAD_BYTES) -> bytes:
+    """QwenQ4ExpertLayerHeader.encode (QwenQ4ExpertStore.swift:76-99)."""
+    h = StoreHeader(layer_index, experts_per_layer, expert_byte_length, payload_byte_length,
+                    payload_sha256.encode(), source_index_sha256.encode())
+    out = (C.c_uint8 * HEADER_BYTES)()
+    _ok(lib().qf_store_header_encode(C.byref(h), out))
+    return bytes(out)
+
+
+def decode_header(data: bytes) -> dict:
+    """QwenQ4ExpertLayerHeader.decode (QwenQ4ExpertStore.swift:101-124)."""
+    buf = (C.c_uint8 * len(data)).from_buffer_copy(data)
+    h = StoreHeader()
+    _ok(lib().qf_store_header_decode(buf, len(data), C.byref(h)))
+    return {"layer_index": h.layer_index, "experts_per_layer": h.experts_per_layer,
+            "expert_byte_length": h.expert_byte_length,
+            "payload_byte_length": h.payload_byte_length,
+            "payload_sha256": h.payload_sha256.decode(),
+            "source_index_sha256": h.source_index_sha256.decode()}
+
+
+def validate_manifest(text: str | bytes) -> None:
+    """QwenQ4ExpertStore.validateManifest (QwenQ4ExpertStore.swift:322-342)."""
+    raw = text.encode() if isinstance(text, str) else bytes(text)
+    _ok(lib().qf_store_validate_manifest(raw, len(raw)))
+
+
+class ExpertStore:
+    """An opened store (QwenQ4ExpertStore.init, QwenQ4ExpertStore.swift:213-282).
+
+    source_index: path of the checkpoint's model.safetensors.index.json, whose
+    SHA-256 must match the manifest; None skips that check."""
+
+    def __init__(self, directory: str, source_index: str | None = None):
+        h = C.c_void_p()
+        _ok(lib().qf_store_open(os.fsencode(directory),
+                                os.fsencode(source_index) if source_index else None, C.byref(h)))
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            lib().qf_store_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def read_expert(self, layer: int, expert: int, out: np.ndarray | None = None) -> np.ndarray:
+        """One record as uint8 [1,769,472] (readExpert, QwenQ4ExpertStore.swift:288-306)."""
+        if out is None:
+            out = np.empty(RECORD_BYTES, dtype=np.uint8)
+        if out.dtype != np.uint8 or out.nbytes < RECORD_BYTES or not out.flags.c_contiguous:
+            raise ValueError("out must be a contiguous uint8 array of >= 1769472 bytes")
+        _ok(lib().qf_store_read_expert(self.h, layer, expert, C.c_void_p(out.ctypes.data)))
+        return out
+
+    def load_tier(self, host_records, first_layer: int = 0, n_layers: int = LAYERS,
+                  threads: int = 8) -> None:
+        """Fill a host tier (uint8 [n_layers * 256, >= RECORD_BYTES], numpy array or
+        CPU torch tensor, pinned for asynchronous copies): record index
+        (layer - first_layer) * 256 + expert."""
+        if hasattr(host_records, "data_ptr"):
+            ptr, shape, stride = host_records.data_ptr(), tuple(host_records.shape), host_records.stride(0)
+            ok = host_records.dtype.__str__() == "torch.uint8" and host_records.stride(1) == 1
+        else:
+            ptr, shape, stride = host_records.ctypes.data, host_records.shape, host_records.strides[0]
+            ok = host_records.dtype == np.uint8 and host_records.strides[1] == 1
+        if not ok or len(shape) != 2 or shape[1] < RECORD_BYTES or shape[0] < n_layers * EXPERTS:
+            raise ValueError("host_records must be uint8 [>= n_layers * 256, >= 1769472], rows contiguous")
+        _ok(lib().qf_store_load_tier(self.h, first_layer, n_layers, C.c_void_p(ptr), stride, threads))
+
+    def verify_layer(self, layer: int) -> bool:
+        """Payload SHA-256 of one layer against the manifest."""
+        m = C.c_int32()
+        _ok(lib().qf_store_verify_layer(self.h, layer, C.byref(m)))
+        return bool(m.value)
+
+    def metrics(self) -> dict:
+        """metricsSnapshot (QwenQ4ExpertStore.swift:308-316)."""
+        m = StoreMetrics()
+        _ok(lib().qf_store_get_metrics(self.h, C.byref(m)))
+        return {"kind": "qwen-q4-packed-v2", "packed_reads": m.packed_reads,
+                "packed_pread_operations": m.pread_operations,
+                "packed_read_failures": m.read_failures}

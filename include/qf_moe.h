@@ -332,9 +332,41 @@ qf_status qf_store_get_metrics(const qf_store *s, qf_store_metrics *out);
 /* SHA-256 of one layer's payload against the manifest digest (the builder's
  * layer check, QwenQ4ExpertStoreBuilder.swift:354-370): *matches = 1 or 0. */
 qf_status qf_store_verify_layer(qf_store *s, int32_t layer, int32_t *matches);
+/* ---- MLX checkpoint (safetensors) loader (host) ----------------------- */
+/* The MoE tensors of one layer, read from the checkpoint the reference runs
+ * (QwenQ4ActiveExpertStreamingRunner.swift:596-620, names resolved through
+ * model.safetensors.index.json's weight_map, shard headers parsed as in
+ * QwenQ4ExpertStoreBuilder.discoverSlices, :202-282), into the host-side
+ * layout of qf_moe_layer:
+ *   mlp.gate.{weight,scales,biases}               -> router_w / router_s / router_b
+ *   mlp.shared_expert_gate.{weight,scales,biases} -> coef_w / coef_s / coef_b
+ *   mlp.shared_expert.{gate,up,down}_proj.*       -> shared_record (one record)
+ *   mlp.switch_mlp.{gate,up,down}_proj.*          -> expert_bank (256 records)
+ * Tensor byte lengths are checked (as the builder does); scales and biases
+ * must all be BF16 or all F16, reported through *scale_dtype.  Any dst
+ * pointer may be NULL to skip that part. */
+typedef struct qf_checkpoint qf_checkpoint;
+typedef struct qf_layer_host {
+    void *router_w;       /* 524,288 bytes: Q8 codes [256][2048] */
+    void *router_s;       /* 16,384 bytes: 16-bit [256][32] */
+    void *router_b;
+    void *coef_w;         /* 2,048 bytes */
+    void *coef_s;         /* 64 bytes */
+    void *coef_b;
+    void *shared_record;  /* 1,769,472 bytes */
+    void *expert_bank;    /* 256 records, record_stride bytes apart */
+    uint64_t record_stride;
+} qf_layer_host;
+/* model_path: the directory holding model.safetensors.index.json and the shards. */
+qf_status qf_checkpoint_open(const char *model_path, qf_checkpoint **out);
+void qf_checkpoint_close(qf_checkpoint *c);
+/* One layer's MoE weights (`threads` readers for the routed records, <= 0: 8). */
+qf_status qf_checkpoint_load_layer(qf_checkpoint *c, int32_t layer, const qf_layer_host *dst,
+                                   int32_t threads, int32_t *scale_dtype);
 /* SHA-256 of n bytes as 64 lowercase hex characters + NUL (out: 65 bytes). */
 qf_status qf_sha256_hex(const void *data, size_t n, char *out);
-/* Message of the last failed qf_store_* / qf_sha256_hex call on this thread. */
+/* Message of the last failed qf_store_* / qf_checkpoint_* / qf_sha256_hex call
+ * on this thread. */
 const char *qf_store_last_error(void);
 
 /* One batch-1 decode step through n_layers MoE blocks whose routed experts

@@ -13,8 +13,12 @@ Restates, from the reference (tanishqpatil/qwen-fieldfare):
     (Sources/QwenFieldfareCore/Storage/QwenQ4ExpertStoreBuilder.swift:284-352),
     with the manifest written as pretty-printed JSON with sorted keys (:168-170);
   - the record read: QwenQ4ExpertStore.readExpert (QwenQ4ExpertStore.swift:288-306).
-A writer that builds stores of full-size layer files needs no 18 GB: records
-that are not given are left as holes of a sparse file (they read as zeros).
+  - the MLX checkpoint the reference runs: safetensors shards behind
+    model.safetensors.index.json, tensor names and shapes of one MoE layer
+    (Sources/QwenFieldfareCore/Runtime/Generation/QwenQ4ActiveExpertStreamingRunner.swift:596-620;
+    switch_mlp slices per expert, QwenQ4ExpertStoreBuilder.swift:41-55, 202-282).
+Writers that build full-size files need no 18 GB: records and slices that are
+not given are left as holes of a sparse file (they read as zeros).
 """
 from __future__ import annotations
 
@@ -151,3 +155,87 @@ def read_expert(directory: str, layer: int, expert: int) -> bytes:
     with open(os.path.join(directory, layer_filename(layer)), "rb") as f:
         f.seek(HEADER_BYTES + expert * RECORD_BYTES)
         return f.read(RECORD_BYTES)
+
+
+# ---- MLX safetensors checkpoint -------------------------------------------
+
+# record components: (suffix, bytes, MLX shape of one expert's tensor, is 16-bit)
+COMPONENTS = [
+    ("gate_proj.weight", 524_288, (512, 256), False), ("gate_proj.scales", 32_768, (512, 32), True),
+    ("gate_proj.biases", 32_768, (512, 32), True),
+    ("up_proj.weight", 524_288, (512, 256), False), ("up_proj.scales", 32_768, (512, 32), True),
+    ("up_proj.biases", 32_768, (512, 32), True),
+    ("down_proj.weight", 524_288, (2048, 64), False), ("down_proj.scales", 32_768, (2048, 8), True),
+    ("down_proj.biases", 32_768, (2048, 8), True),
+]
+COMPONENT_OFFSETS = [0, 524_288, 557_056, 589_824, 1_114_112, 1_146_880, 1_179_648, 1_703_936, 1_736_704]
+
+
+class Sparse:
+    """A tensor of `size` bytes of which only `pieces` {offset: bytes} are data."""
+
+    def __init__(self, size: int, pieces: dict[int, bytes]):
+        self.size, self.pieces = size, pieces
+
+
+def split_record(record: bytes) -> list[bytes]:
+    return [record[o:o + n] for o, (_, n, _, _) in zip(COMPONENT_OFFSETS, COMPONENTS)]
+
+
+def moe_layer_tensors(layer: int, router_w: bytes, router_s: bytes, router_b: bytes, coef_w: bytes,
+                      coef_s: bytes, coef_b: bytes, shared_record: bytes, bank: dict[int, bytes],
+                      scale_dtype: str = "F16") -> dict:
+    """name -> (dtype, shape, bytes | Sparse) for one layer's MoE tensors."""
+    pre = f"language_model.model.layers.{layer}.mlp."
+    t = {pre + "gate.weight": ("U32", (256, 512), router_w),
+         pre + "gate.scales": (scale_dtype, (256, 32), router_s),
+         pre + "gate.biases": (scale_dtype, (256, 32), router_b),
+         pre + "shared_expert_gate.weight": ("U32", (1, 512), coef_w),
+         pre + "shared_expert_gate.scales": (scale_dtype, (1, 32), coef_s),
+         pre + "shared_expert_gate.biases": (scale_dtype, (1, 32), coef_b)}
+    for (suffix, n, shape, is16), part in zip(COMPONENTS, split_record(shared_record)):
+        t[pre + "shared_expert." + suffix] = (scale_dtype if is16 else "U32", shape, part)
+    for k, (suffix, n, shape, is16) in enumerate(COMPONENTS):
+        pieces = {e * n: split_record(rec)[k] for e, rec in bank.items()}
+        t[pre + "switch_mlp." + suffix] = (scale_dtype if is16 else "U32", (256,) + shape,
+                                           Sparse(256 * n, pieces))
+    return t
+
+
+def write_safetensors(path: str, tensors: dict) -> None:
+    """safetensors: u64 little-endian header length, JSON header with
+    data_offsets relative to the data, header padded with spaces to 8 bytes."""
+    header, off = {}, 0
+    for name, (dtype, shape, data) in tensors.items():
+        n = data.size if isinstance(data, Sparse) else len(data)
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + n]}
+        off += n
+    hj = json.dumps(header, separators=(",", ":")).encode()
+    hj += b" " * (-len(hj) % 8)
+    base = 8 + len(hj)
+    with open(path, "wb") as f:
+        f.truncate(base + off)
+        f.write(struct.pack("<Q", len(hj)) + hj)
+        for name, (dtype, shape, data) in tensors.items():
+            start = base + header[name]["data_offsets"][0]
+            if isinstance(data, Sparse):
+                for o, piece in data.pieces.items():
+                    f.seek(start + o)
+                    f.write(piece)
+            else:
+                f.seek(start)
+                f.write(data)
+
+
+def write_checkpoint(model_dir: str, tensors: dict, n_shards: int = 2) -> None:
+    """Tensors spread round-robin over n_shards files, with the index."""
+    os.makedirs(model_dir, exist_ok=True)
+    names = list(tensors)
+    shard_names = [f"model-{i + 1:05d}-of-{n_shards:05d}.safetensors" for i in range(n_shards)]
+    weight_map = {}
+    for i, sn in enumerate(shard_names):
+        mine = {n: tensors[n] for n in names[i::n_shards]}
+        write_safetensors(os.path.join(model_dir, sn), mine)
+        weight_map.update({n: sn for n in mine})
+    with open(os.path.join(model_dir, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": 0}, "weight_map": weight_map}, f, indent=2)

@@ -501,6 +501,90 @@ bool hash_file(const std::string& path, std::string& hex) {
   return true;
 }
 
+// ---------------------------------------------------------------- checkpoint
+// MLX safetensors shards: u64 little-endian header length, JSON header
+// {name: {"dtype", "shape", "data_offsets": [begin, end]}}, then the data.
+struct Slice {
+  int fd = -1;
+  uint64_t offset = 0;  // absolute file offset
+  uint64_t bytes = 0;
+  std::string dtype;
+};
+
+struct Shard {
+  std::string path;
+  int fd = -1;
+  bool parsed = false;
+  std::map<std::string, Slice> tensors;
+};
+
+// the 9 record components in record order (QwenQ4ExpertStoreBuilder.swift:41-55)
+const char* const kComponentSuffix[9] = {"gate_proj.weight", "gate_proj.scales", "gate_proj.biases",
+                                         "up_proj.weight",   "up_proj.scales",   "up_proj.biases",
+                                         "down_proj.weight", "down_proj.scales", "down_proj.biases"};
+const uint64_t kComponentBytes[9] = {524288, 32768, 32768, 524288, 32768, 32768, 524288, 32768, 32768};
+const uint64_t kComponentOffset[9] = {0, 524288, 557056, 589824, 1114112, 1146880, 1179648, 1703936, 1736704};
+
+}  // namespace
+
+struct qf_checkpoint {
+  std::string dir;
+  std::map<std::string, std::string> weight_map;  // tensor name -> shard file
+  std::map<std::string, Shard> shards;             // shard file -> parsed header + fd
+  ~qf_checkpoint() {
+    for (auto& kv : shards)
+      if (kv.second.fd >= 0) ::close(kv.second.fd);
+  }
+  // the tensor's slice; QwenQ4ExpertStoreBuilder.discoverSlices (:202-282)
+  qf_status find(const std::string& name, Slice& out) {
+    auto w = weight_map.find(name);
+    if (w == weight_map.end()) return fail(QF_ERR_ARG, "invalid manifest: source index is missing " + name);
+    Shard& sh = shards[w->second];
+    if (!sh.parsed) {
+      sh.path = dir + "/" + w->second;
+      sh.fd = ::open(sh.path.c_str(), O_RDONLY | O_CLOEXEC | O_NOFOLLOW);
+      if (sh.fd < 0) return fail(QF_ERR_IO, "open failed for " + sh.path + ": errno " + std::to_string(errno));
+      uint8_t lb[8];
+      if (pread_fully(sh.fd, lb, 8, 0) != 8) return fail(QF_ERR_IO, "short read from " + sh.path);
+      const uint64_t hlen = get64(lb);
+      if (hlen == 0 || hlen > (256ull << 20))
+        return fail(QF_ERR_ARG, "invalid manifest: invalid safetensors header length in " + w->second);
+      std::string text(hlen, '\0');
+      if (pread_fully(sh.fd, &text[0], hlen, 8) != hlen) return fail(QF_ERR_IO, "short read from " + sh.path);
+      Json root;
+      if (!JsonParser(text.data(), text.size()).parse(root) || root.kind != Json::Obj)
+        return fail(QF_ERR_ARG, "invalid manifest: invalid safetensors header in " + w->second);
+      for (auto& kv : root.obj) {
+        if (kv.first == "__metadata__" || kv.second.kind != Json::Obj) continue;
+        auto off = kv.second.obj.find("data_offsets");
+        if (off == kv.second.obj.end() || off->second.kind != Json::Arr || off->second.arr.size() != 2 ||
+            !off->second.arr[0].integral || !off->second.arr[1].integral)
+          continue;
+        const int64_t b = off->second.arr[0].i, e = off->second.arr[1].i;
+        if (b < 0 || e < b) continue;
+        Slice sl;
+        sl.fd = sh.fd;
+        sl.offset = 8 + hlen + (uint64_t)b;
+        sl.bytes = (uint64_t)(e - b);
+        get_str(kv.second, "dtype", sl.dtype);
+        sh.tensors[kv.first] = sl;
+      }
+      sh.parsed = true;
+    }
+    auto t = sh.tensors.find(name);
+    if (t == sh.tensors.end()) return fail(QF_ERR_ARG, "invalid manifest: missing tensor metadata for " + name);
+    out = t->second;
+    return QF_OK;
+  }
+};
+
+namespace {
+
+qf_status read_slice(const Slice& sl, uint64_t at, void* dst, uint64_t n, const std::string& name) {
+  if (pread_fully(sl.fd, dst, n, sl.offset + at) != n) return fail(QF_ERR_IO, "short read of " + name);
+  return QF_OK;
+}
+
 }  // namespace
 
 struct qf_store {
@@ -708,6 +792,129 @@ qf_status qf_store_verify_layer(qf_store* s, int32_t layer, int32_t* matches) {
     left -= got;
   }
   *matches = h.hex() == s->manifest.layers[layer].payload_sha256 ? 1 : 0;
+  return QF_OK;
+}
+
+qf_status qf_checkpoint_open(const char* model_path, qf_checkpoint** out) {
+  if (!model_path || !out) return fail(QF_ERR_ARG, "qf_checkpoint_open: null pointer");
+  *out = nullptr;
+  std::unique_ptr<qf_checkpoint> c(new qf_checkpoint);
+  c->dir = model_path;
+  const std::string ipath = c->dir + "/model.safetensors.index.json";
+  std::string text;
+  if (!read_file(ipath, text)) return fail(QF_ERR_IO, "open failed for " + ipath + ": errno " + std::to_string(errno));
+  Json root;
+  if (!JsonParser(text.data(), text.size()).parse(root) || root.kind != Json::Obj)
+    return fail(QF_ERR_ARG, "invalid manifest: source index is not a JSON object");
+  auto wm = root.obj.find("weight_map");
+  if (wm == root.obj.end() || wm->second.kind != Json::Obj)
+    return fail(QF_ERR_ARG, "invalid manifest: source index has no weight_map");
+  for (auto& kv : wm->second.obj) {
+    if (kv.second.kind != Json::Str || kv.second.s.empty() || kv.second.s.find('/') != std::string::npos)
+      return fail(QF_ERR_ARG, "invalid manifest: bad shard name for " + kv.first);
+    c->weight_map[kv.first] = kv.second.s;
+  }
+  *out = c.release();
+  return QF_OK;
+}
+
+void qf_checkpoint_close(qf_checkpoint* c) { delete c; }
+
+qf_status qf_checkpoint_load_layer(qf_checkpoint* c, int32_t layer, const qf_layer_host* dst, int32_t threads,
+                                   int32_t* scale_dtype) {
+  if (!c || !dst) return fail(QF_ERR_ARG, "qf_checkpoint_load_layer: null pointer");
+  if (layer < 0 || layer >= kLayers) return fail(QF_ERR_ARG, "qf_checkpoint_load_layer: layer out of range");
+  if (dst->expert_bank && dst->record_stride < kRecordBytes)
+    return fail(QF_ERR_ARG, "qf_checkpoint_load_layer: record_stride below one record");
+  const std::string pre = "language_model.model.layers." + std::to_string(layer) + ".mlp.";
+  struct Want {
+    std::string name;
+    uint64_t bytes;
+    void* dst;
+    bool scales;  // a 16-bit scale or bias tensor
+  };
+  // QwenQ4ActiveExpertStreamingRunner.swift:596-614 (router, shared gate, shared expert)
+  std::vector<Want> direct = {
+      {pre + "gate.weight", 256 * 2048, dst->router_w, false},
+      {pre + "gate.scales", 256 * 32 * 2, dst->router_s, true},
+      {pre + "gate.biases", 256 * 32 * 2, dst->router_b, true},
+      {pre + "shared_expert_gate.weight", 2048, dst->coef_w, false},
+      {pre + "shared_expert_gate.scales", 32 * 2, dst->coef_s, true},
+      {pre + "shared_expert_gate.biases", 32 * 2, dst->coef_b, true},
+  };
+  std::string dtype16;
+  auto check16 = [&](const Want& w, const Slice& sl) -> qf_status {
+    if (!w.scales) return QF_OK;
+    if (sl.dtype != "BF16" && sl.dtype != "F16")
+      return fail(QF_ERR_ARG, "invalid manifest: " + w.name + " is " + sl.dtype + ", not BF16 or F16");
+    if (dtype16.empty()) dtype16 = sl.dtype;
+    if (sl.dtype != dtype16) return fail(QF_ERR_ARG, "invalid manifest: mixed scale types in layer " + std::to_string(layer));
+    return QF_OK;
+  };
+  auto sized = [&](const Want& w, const Slice& sl, uint64_t expected) -> qf_status {
+    if (sl.bytes != expected)
+      return fail(QF_ERR_ARG, "invalid manifest: unexpected byte length for " + w.name + ": expected " +
+                                  std::to_string(expected) + ", got " + std::to_string(sl.bytes));
+    return check16(w, sl);
+  };
+  std::vector<std::pair<Want, Slice>> plain;
+  for (const Want& w : direct) {
+    Slice sl;
+    qf_status st = c->find(w.name, sl);
+    if (st == QF_OK) st = sized(w, sl, w.bytes);
+    if (st != QF_OK) return st;
+    plain.push_back({w, sl});
+  }
+  // shared expert: one record (QwenQ4ActiveExpertStreamingRunner.swift:605-613)
+  for (int k = 0; k < 9; k++) {
+    Want w{pre + "shared_expert." + kComponentSuffix[k], kComponentBytes[k],
+           dst->shared_record ? static_cast<uint8_t*>(dst->shared_record) + kComponentOffset[k] : nullptr, k % 3 != 0};
+    Slice sl;
+    qf_status st = c->find(w.name, sl);
+    if (st == QF_OK) st = sized(w, sl, w.bytes);
+    if (st != QF_OK) return st;
+    plain.push_back({w, sl});
+  }
+  // routed experts: [256][component] slices packed into records (builder packLayer, :284-327)
+  Slice sw[9];
+  std::string swname[9];
+  for (int k = 0; k < 9; k++) {
+    swname[k] = pre + "switch_mlp." + kComponentSuffix[k];
+    Want w{swname[k], 0, nullptr, k % 3 != 0};
+    qf_status st = c->find(w.name, sw[k]);
+    if (st == QF_OK) st = sized(w, sw[k], kComponentBytes[k] * kExpertsPerLayer);
+    if (st != QF_OK) return st;
+  }
+  for (auto& pw : plain)
+    if (pw.first.dst) {
+      const qf_status st = read_slice(pw.second, 0, pw.first.dst, pw.first.bytes, pw.first.name);
+      if (st != QF_OK) return st;
+    }
+  if (dst->expert_bank) {
+    const int nt = std::max(1, std::min(threads > 0 ? threads : 8, 64));
+    std::atomic<int> next{0};
+    std::atomic<int> bad{-1};
+    auto work = [&]() {
+      for (;;) {
+        const int e = next.fetch_add(1);
+        if (e >= kExpertsPerLayer) return;
+        uint8_t* rec = static_cast<uint8_t*>(dst->expert_bank) + (uint64_t)e * dst->record_stride;
+        for (int k = 0; k < 9; k++)
+          if (pread_fully(sw[k].fd, rec + kComponentOffset[k], kComponentBytes[k],
+                          sw[k].offset + (uint64_t)e * kComponentBytes[k]) != kComponentBytes[k]) {
+            int expect = -1;
+            bad.compare_exchange_strong(expect, e * 9 + k);
+          }
+      }
+    };
+    std::vector<std::thread> pool;
+    for (int t = 1; t < nt; t++) pool.emplace_back(work);
+    work();
+    for (auto& t : pool) t.join();
+    if (bad.load() >= 0)
+      return fail(QF_ERR_IO, "short read of " + swname[bad.load() % 9] + " expert " + std::to_string(bad.load() / 9));
+  }
+  if (scale_dtype) *scale_dtype = dtype16 == "BF16" ? QF_SCALE_BF16 : QF_SCALE_F16;
   return QF_OK;
 }
 

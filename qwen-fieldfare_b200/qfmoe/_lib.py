@@ -62,6 +62,12 @@ class StoreMetrics(C.Structure):
                 ("read_failures", C.c_int64)]
 
 
+class LayerHost(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("router_w", "router_s", "router_b", "coef_w", "coef_s",
+                                          "coef_b", "shared_record", "expert_bank")] + \
+               [("record_stride", C.c_uint64)]
+
+
 # (name, restype, argtypes) for every symbol include/qf_moe.h declares.
 _P = C.c_void_p
 _I = C.c_int32
@@ -128,6 +134,9 @@ SIGNATURES = {
     "qf_store_verify_layer": (_S, [_P, _I, C.POINTER(_I)]),
     "qf_sha256_hex": (_S, [_P, C.c_size_t, _P]),
     "qf_store_last_error": (C.c_char_p, []),
+    "qf_checkpoint_open": (_S, [C.c_char_p, C.POINTER(_P)]),
+    "qf_checkpoint_close": (None, [_P]),
+    "qf_checkpoint_load_layer": (_S, [_P, _I, C.POINTER(LayerHost), _I, C.POINTER(_I)]),
 }
 
 _lib = None

@@ -13,7 +13,7 @@ import os
 
 import numpy as np
 
-from ._lib import QF_OK, QfError, StoreHeader, StoreMetrics, lib
+from ._lib import QF_OK, LayerHost, QfError, StoreHeader, StoreMetrics, lib
 from .moe import EXPERTS, RECORD_BYTES
 
 HEADER_BYTES = 4096
@@ -135,3 +135,64 @@ class ExpertStore:
         return {"kind": "qwen-q4-packed-v2", "packed_reads": m.packed_reads,
                 "packed_pread_operations": m.pread_operations,
                 "packed_read_failures": m.read_failures}
+
+
+class Checkpoint:
+    """The MoE tensors of an MLX safetensors checkpoint (qf_checkpoint_*): the
+    directory holds model.safetensors.index.json and its shards
+    (QwenQ4ActiveExpertStreamingRunner.swift:596-620)."""
+
+    def __init__(self, model_path: str):
+        h = C.c_void_p()
+        _ok(lib().qf_checkpoint_open(os.fsencode(model_path), C.byref(h)))
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            lib().qf_checkpoint_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_layer(self, layer: int, with_bank: bool = True, threads: int = 8):
+        """One layer in the host layout of qf_moe_layer: a dict of uint8 numpy
+        arrays (router_w, router_s, router_b, coef_w, coef_s, coef_b, shared,
+        bank [256, RECORD_BYTES] or None) and the scale dtype ("bf16" | "f16")."""
+        out = {"router_w": np.empty(EXPERTS * 2048, np.uint8),
+               "router_s": np.empty(EXPERTS * 64, np.uint8), "router_b": np.empty(EXPERTS * 64, np.uint8),
+               "coef_w": np.empty(2048, np.uint8), "coef_s": np.empty(64, np.uint8),
+               "coef_b": np.empty(64, np.uint8), "shared": np.empty(RECORD_BYTES, np.uint8),
+               "bank": np.empty((EXPERTS, RECORD_BYTES), np.uint8) if with_bank else None}
+        ptr = {k: (C.c_void_p(v.ctypes.data) if v is not None else None) for k, v in out.items()}
+        d = LayerHost(ptr["router_w"], ptr["router_s"], ptr["router_b"], ptr["coef_w"], ptr["coef_s"],
+                      ptr["coef_b"], ptr["shared"], ptr["bank"], RECORD_BYTES)
+        dt = C.c_int32()
+        _ok(lib().qf_checkpoint_load_layer(self.h, layer, C.byref(d), threads, C.byref(dt)))
+        return out, ("bf16" if dt.value == 1 else "f16")
+
+    def layer_weights(self, ctx, layer: int, threads: int = 8):
+        """The layer as device-resident MoELayerWeights, and its scale dtype."""
+        import torch
+        from .moe import MoELayerWeights
+        host, dtype = self.load_layer(layer, True, threads)
+        if (dtype == "bf16") != bool(ctx.scale_bf16):
+            raise ValueError(f"checkpoint scales are {dtype}; create the MoEContext with "
+                             f"scale_bf16={dtype == 'bf16'}")
+        dev = ctx.device
+
+        def up(a, i16=False):
+            t = torch.from_numpy(a)
+            return (t.view(torch.int16) if i16 else t).to(dev)
+        return MoELayerWeights(up(host["router_w"]), up(host["router_s"], True), up(host["router_b"], True),
+                               up(host["coef_w"]), up(host["coef_s"], True), up(host["coef_b"], True),
+                               up(host["shared"]), up(host["bank"])), dtype

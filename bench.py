@@ -524,6 +524,38 @@ def main():
                 "remote_rows_sent_rank0": sent_remote,
                 "dispatch_remote_bytes_rank0": sent_remote * 4096}
 
+    def measure_lm_head(steps: int, warmup: int):
+        """Q4 LM head of the 248,320-row vocabulary for one token row (the last
+        GEMV of a decode step): 286 MB of weights, larger than L2."""
+        rows = 248_320
+        gen = torch.Generator(device=dev).manual_seed(5)
+        w = torch.randint(0, 256, (rows, 1024), dtype=torch.uint8, device=dev, generator=gen)
+        sc = torch.randn((rows, 32), device=dev, generator=gen).abs() * 0.01 + 1e-3
+        s, b = sc.half().view(torch.int16), (-8 * sc).half().view(torch.int16)
+        x = torch.randn((1, 2048), device=dev, generator=gen)
+        x = x / x.pow(2).mean().sqrt()
+        out = torch.empty((1, rows), device=dev)
+        for _ in range(warmup):
+            Q.lm_head(ctx, w, s, b, x, out=out)
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(steps):
+            Q.lm_head(ctx, w, s, b, x, out=out)
+        ev1.record()
+        ev1.synchronize()
+        ctx.check()
+        ms = ev0.elapsed_time(ev1) / steps
+        nbytes = rows * (1024 + 64 + 64) + 2048 * 4 + rows * 4
+        gbs = nbytes / (ms / 1e3) / 1e9
+        return {"workload": "Q4 LM head, 248,320 x 2,048, one fp32 token row, fp16 scales "
+                            "(deltanet.metal:1897-1919 as dispatched at QwenQ4ActiveExpertStreamingRunner.swift:1393-1400)",
+                "ms_per_token": ms, "launches": steps,
+                "roofline": {"bound": "hbm", "kernel": "k_lm_head", "achieved": gbs, "peak": hbm_peak,
+                             "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": peak_kind,
+                             "bytes_per_launch": nbytes}}
+
     def ep_line(r):
         _, tc_peak, tc_kind = peaks()
         gemm_ms = r["kernel_ms"]["gate_up"] + r["kernel_ms"]["down"]
@@ -626,6 +658,7 @@ def main():
     cst = None if (args.no_cache_stream or world > 1) else measure_cache_stream(
         args.cache_tokens, args.cache_slots, args.cache_policy)
     epr = None if args.no_ep else measure_ep(args.ep_tokens, 20, 3)
+    lmh = None if args.no_extras else measure_lm_head(50, 5)
 
     if rank == 0:
         cpu = None
@@ -686,6 +719,8 @@ def main():
             line["cache_stream"] = cache_line(cst)
         if epr is not None:
             line["ep_16k"] = ep_line(epr)
+        if lmh is not None:
+            line["lm_head"] = lmh
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -123,6 +123,18 @@ int qf_moe_abi_version(void);
 qf_status qf_router_logits_q8(qf_moe *h, const qf_moe_layer *layer, int32_t T,
                               const uint16_t *x, float *logits, float *coef);
 
+/* Q4 LM head: logits[t][r] = row r of W (rows x 2048, MLX-affine Q4, group
+ * 64) dotted with the fp32 row x[t] (the final RMSNorm output), for T token
+ * rows.  Replaces deltanet.metal:1897-1919 qwen_gemv_q4_affine_simd_f32 as
+ * dispatched for the 248,320-row LM head at
+ * QwenQ4ActiveExpertStreamingRunner.swift:1393-1400, with the same per-lane
+ * arithmetic order (bit-exact with the CPU oracle).  w [rows][1024] bytes,
+ * scales / biases [rows][32] 16-bit in the handle's scale dtype, x [T][2048]
+ * (w, scales, biases and x 16-B aligned), logits [T][rows]; the weights
+ * stream once per token row. */
+qf_status qf_lm_head_q4(qf_moe *h, const void *w, const void *scales, const void *biases, int32_t rows,
+                        int32_t T, const float *x, float *logits);
+
 /* Top-k by logit (ties to the lower expert index), softmax over all experts,
  * renormalised over the top-k.  Replaces qwen_router_top8_logits_f32
  * (deltanet.metal:2283-2329, dispatched at runner :1186-1190).

@@ -81,6 +81,7 @@ def _declare(L):
     L.qfo_gate_up.argtypes = [_p, _i, _p, _p]
     L.qfo_down.argtypes = [_p, _i, _p, _p]
     L.qfo_combine.argtypes = [_p, _p, _p, C.c_float, _p, _p]
+    L.qfo_lm_head.argtypes = [_p, _p, _p, _i, _p, _i, _p]
 
 
 def _ptr(a):
@@ -385,3 +386,17 @@ def plan_slots(budget_gib: int, context_length: int):
     target = budget_gib * GIB
     slots = max(0, target - non_cache) // RECORD_BYTES
     return slots, non_cache + slots * RECORD_BYTES, target, slots >= layers * 8
+
+
+def lm_head(w: np.ndarray, s: np.ndarray, b: np.ndarray, x: np.ndarray, bf16: bool = False) -> np.ndarray:
+    """Q4 LM-head logits of one fp32 token row (qfo_lm_head, reference order):
+    w uint8 [rows, 1024], s/b uint16 bits [rows, 32], x float32 [2048]."""
+    w = np.ascontiguousarray(w, np.uint8)
+    s = np.ascontiguousarray(s, np.uint16)
+    b = np.ascontiguousarray(b, np.uint16)
+    x = np.ascontiguousarray(x, np.float32)
+    rows = w.shape[0]
+    assert w.shape == (rows, 1024) and s.shape == (rows, 32) and b.shape == (rows, 32) and x.shape == (2048,)
+    out = np.empty(rows, np.float32)
+    lib().qfo_lm_head(_ptr(w), _ptr(s), _ptr(b), rows, _ptr(x), int(bf16), _ptr(out))
+    return out

@@ -289,6 +289,17 @@ float qfo_q8_row(const uint8_t *w_row, const uint16_t *s_row, const uint16_t *b_
     return butterfly32(lane_acc);
 }
 
+/* deltanet.metal:1897-1919 qwen_gemv_q4_affine_simd_f32: one 32-lane row per
+ * SIMD group, rows independent (the LM head at cols = 2048) */
+void qfo_lm_head(const uint8_t *w, const uint16_t *s, const uint16_t *b, int rows, const float *x,
+                 int scale_bf16, float *out) {
+#ifdef _OPENMP
+#pragma omp parallel for if (!omp_in_parallel()) schedule(static)
+#endif
+    for (int r = 0; r < rows; r++)
+        out[r] = qfo_q4_row(w + (size_t)r * 1024, s + (size_t)r * 32, b + (size_t)r * 32, x, 2048, scale_bf16);
+}
+
 /* deltanet.metal:2262-2281 qwen_router_q8_logits_simd_f32 */
 void qfo_router_logits(const qfo_layer *L, const float *x, float *logits) {
 #ifdef _OPENMP

@@ -100,6 +100,11 @@ float qfo_q4_row(const uint8_t *w_row, const uint16_t *s_row, const uint16_t *b_
 float qfo_q8_row(const uint8_t *w_row, const uint16_t *s_row, const uint16_t *b_row,
                  const float *vec, int scale_bf16);
 void qfo_router_logits(const qfo_layer *L, const float *x, float *logits);
+/* deltanet.metal:1897-1919 qwen_gemv_q4_affine_simd_f32 with cols 2048, the
+ * LM head (QwenQ4ActiveExpertStreamingRunner.swift:1393-1400): out[r] =
+ * qfo_q4_row of row r; w [rows][1024], s/b [rows][32] */
+void qfo_lm_head(const uint8_t *w, const uint16_t *s, const uint16_t *b, int rows, const float *x,
+                 int scale_bf16, float *out);
 /* top-k by logit (ties -> lower index), softmax over all, renormalise over top-k */
 void qfo_topk(const float *logits, const float *bias, int n, int k, int32_t *idx, float *w);
 float qfo_coef(const qfo_layer *L, const float *x);

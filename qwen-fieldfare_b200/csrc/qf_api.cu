@@ -194,6 +194,24 @@ qf_status qf_router_logits_q8(qf_moe* h, const qf_moe_layer* layer, int32_t T, c
   return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_router_logits_q8");
 }
 
+qf_status qf_lm_head_q4(qf_moe* h, const void* w, const void* scales, const void* biases, int32_t rows,
+                        int32_t T, const float* x, float* logits) {
+  if (!h) return QF_ERR_ARG;
+  if (rows < 1 || T < 1 || T > 64) return fail(h, QF_ERR_ARG, "rows must be >= 1 and T in [1, 64]");
+  if (!w || !scales || !biases || !x || !logits || !aligned(w, 16) || !aligned(scales, 16) ||
+      !aligned(biases, 16) || !aligned(x, 16))
+    return fail(h, QF_ERR_ARG, "w, scales, biases and x (16-B aligned) and logits are required");
+  DeviceGuard g(h->device);
+  int sms = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->device);
+  const bool bf16 = h->dims.scale_dtype == QF_SCALE_BF16;
+  // one token row per launch: the weights stream once per token
+  for (int t = 0; t < T && e == cudaSuccess; t++)
+    e = qf::lm_head_q4(stream_of(h), bf16, w, scales, biases, rows, x + (size_t)t * 2048,
+                       logits + (size_t)t * rows, sms);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_lm_head_q4");
+}
+
 qf_status qf_router_topk(qf_moe* h, const float* logits, const float* bias, int32_t T, int32_t* idx,
                          float* w) {
   if (!h) return QF_ERR_ARG;

@@ -85,6 +85,10 @@ cudaError_t decode_block(cudaStream_t st, const LayerW& L, bool bf16, int T, con
                          float* w_out, const DecodeWs& ws, uint16_t* x16_next, float eps,
                          int* status, Prof* prof);
 
+// ---- Q4 LM head (qf_lmhead.cu): logits of one fp32 row, rows x 2048 Q4 g64
+cudaError_t lm_head_q4(cudaStream_t st, bool bf16, const void* w, const void* s, const void* b, int rows,
+                       const float* x, float* out, int sms);
+
 cudaError_t router_logits(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
                           float* logits, float* coef, int* status);
 cudaError_t router_topk(cudaStream_t st, int T, const float* logits, const float* bias,

@@ -181,6 +181,23 @@ def router_topk(ctx: MoEContext, logits: torch.Tensor, bias: torch.Tensor | None
     return idx, w
 
 
+def lm_head(ctx: MoEContext, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+            x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Q4 LM-head logits (qwen_gemv_q4_affine_simd_f32, reference order): w uint8
+    [rows, 1024], scales / biases int16 bits [rows, 32] in the context's scale
+    dtype, x fp32 [T, 2048] -> logits fp32 [T, rows]."""
+    rows = w.shape[0]
+    if x.dim() == 1:
+        x = x[None]
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, rows), dtype=torch.float32, device=ctx.device)
+    ctx._bind_stream()
+    check(lib().qf_lm_head_q4(ctx.h, _ptr(w), _ptr(scales), _ptr(biases), rows, T, _ptr(x), _ptr(out)),
+          ctx.h)
+    return out
+
+
 def dispatch_plan(ctx: MoEContext, idx: torch.Tensor):
     """Stable dispatch plan: counts [256], offsets [257], perm [T*8] (by expert, token, k)."""
     T = idx.shape[0]

@@ -27,7 +27,8 @@
 //   - Rows stream through a per-warp shared-memory ring of 4 stages filled
 //     by cp.async (16-byte pieces, no registers held): 4 rows in flight per
 //     warp; each lane then reads its code words from the stage without bank
-//     conflicts (word blk*32 + lane).
+//     conflicts (word blk*32 + lane).  A warp reduces two rows per iteration
+//     (8 independent chains), 128 registers, 4 blocks of 4 warps per SM.
 
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -135,49 +136,68 @@ __global__ void __launch_bounds__(kLmThreads) k_lm_head(const uint8_t* __restric
   }
   const uint64_t neg_magic = pk(-8388608.0f, -8388608.0f);
   const uint64_t minus1 = pk(-1.0f, -1.0f);
+  // two rows per iteration (stages 2k and 2k+1 of the ring): twice the
+  // independent chains per warp
   int stage = 0;
-  for (int r = r0; r < rows; r += nwarps) {
-    cp_wait<kLmStages - 1>();  // this lane's pieces of the oldest row have landed
-    __syncwarp();              // and every lane's
-    const uint8_t* st = ring[wib][stage];
-    const uint32_t* cw = reinterpret_cast<const uint32_t*>(st);
-    uint32_t c[8];
+  for (int r = r0; r < rows; r += 2 * nwarps) {
+    const int r2 = r + nwarps;
+    cp_wait<kLmStages - 2>();
+    __syncwarp();
+    uint32_t c[2][8];
+    float sl[2], bl[2];
 #pragma unroll
-    for (int blk = 0; blk < 8; blk++) c[blk] = cw[blk * 32 + lane];
-    const float sl = s16<BF16>(reinterpret_cast<const uint16_t*>(st + 1024)[lane]);
-    const float bl = s16<BF16>(reinterpret_cast<const uint16_t*>(st + 1088)[lane]);
-    __syncwarp();  // the stage is read: refill it with the row kLmStages ahead
+    for (int q = 0; q < 2; q++) {
+      const uint8_t* st = ring[wib][stage + q];
+      const uint32_t* cw = reinterpret_cast<const uint32_t*>(st);
+#pragma unroll
+      for (int blk = 0; blk < 8; blk++) c[q][blk] = cw[blk * 32 + lane];
+      sl[q] = s16<BF16>(reinterpret_cast<const uint16_t*>(st + 1024)[lane]);
+      bl[q] = s16<BF16>(reinterpret_cast<const uint16_t*>(st + 1088)[lane]);
+    }
+    __syncwarp();
     issue_row(ring[wib][stage], w, s, b, r + kLmStages * nwarps, rows, lane);
-    stage = stage + 1 == kLmStages ? 0 : stage + 1;
-    float acc = 0.0f;
+    issue_row(ring[wib][stage + 1], w, s, b, r2 + kLmStages * nwarps, rows, lane);
+    stage = stage + 2 == kLmStages ? 0 : stage + 2;
+    float acc[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int p = 0; p < 4; p++) {
-      uint64_t dot = 0;  // (+0, +0)
+      uint64_t dot[2] = {0, 0};  // (+0, +0)
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        // 2^23 + byte j of each block's word, then 2^23 + its low nibble
-        const uint32_t a0 = __byte_perm(c[2 * p], 0x4B000000u, 0x7540u | j);
-        const uint32_t a1 = __byte_perm(c[2 * p + 1], 0x4B000000u, 0x7540u | j);
-        const uint64_t A = (uint64_t)a0 | ((uint64_t)a1 << 32);
-        const uint64_t L = A & 0xFFFFFF0FFFFFFF0Full;
-        const uint64_t lo = add2(L, neg_magic);    // q of the low nibble
-        const uint64_t hi16 = fma2(L, minus1, A);  // 16 q of the high nibble
-        dot = fma2(lo, ev[p][j], dot);
-        dot = fma2(hi16, od[p][j], dot);
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          const uint32_t a0 = __byte_perm(c[q][2 * p], 0x4B000000u, 0x7540u | j);
+          const uint32_t a1 = __byte_perm(c[q][2 * p + 1], 0x4B000000u, 0x7540u | j);
+          const uint64_t A = (uint64_t)a0 | ((uint64_t)a1 << 32);
+          const uint64_t L = A & 0xFFFFFF0FFFFFFF0Full;
+          const uint64_t lo = add2(L, neg_magic);
+          const uint64_t hi16 = fma2(L, minus1, A);
+          dot[q] = fma2(lo, ev[p][j], dot[q]);
+          dot[q] = fma2(hi16, od[p][j], dot[q]);
+        }
       }
 #pragma unroll
       for (int h = 0; h < 2; h++) {
         const int blk = 2 * p + h;
         const int g = blk * 4 + (lane >> 3);
-        const float sc = __shfl_sync(0xffffffffu, sl, g);
-        const float bi = __shfl_sync(0xffffffffu, bl, g);
-        acc = __fmaf_rn(sc, h ? hi32(dot) : lo32(dot), acc);
-        acc = __fmaf_rn(bi, esum[blk], acc);
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          const float sc = __shfl_sync(0xffffffffu, sl[q], g);
+          const float bi = __shfl_sync(0xffffffffu, bl[q], g);
+          acc[q] = __fmaf_rn(sc, h ? hi32(dot[q]) : lo32(dot[q]), acc[q]);
+          acc[q] = __fmaf_rn(bi, esum[blk], acc[q]);
+        }
       }
     }
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-    if (lane == 0) out[r] = acc;
+    for (int m = 16; m >= 1; m >>= 1) {
+      acc[0] = __fadd_rn(acc[0], __shfl_xor_sync(0xffffffffu, acc[0], m));
+      acc[1] = __fadd_rn(acc[1], __shfl_xor_sync(0xffffffffu, acc[1], m));
+    }
+    if (lane == 0) {
+      out[r] = acc[0];
+      if (r2 < rows) out[r2] = acc[1];
+    }
   }
   cp_wait<0>();  // no copy in flight when the warp exits
 }

@@ -178,3 +178,31 @@ def test_golden_fixture_config0():
     assert np.allclose(r["w"], np.array(g["w"], np.float32), rtol=0, atol=0)
     assert hashlib.sha256(r["out"].tobytes()).hexdigest() == g["out_sha256"]
     assert hashlib.sha256(x.tobytes()).hexdigest() == g["x_sha256"]
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_lm_head_rows_match_float64(bf16):
+    """qfo_lm_head (the reference GEMV's per-lane order) against an fp64
+    evaluation of sum_g s_g * sum_k q_k x_k + b_g * sum_k x_k, row by row."""
+    rng = np.random.default_rng(12 + bf16)
+    rows = 300
+    w = rng.integers(0, 256, (rows, 1024), dtype=np.uint8)
+    s32 = (np.abs(rng.normal(0, 0.01, (rows, 32))) + 1e-3).astype(np.float32)
+    b32 = (-8 * s32).astype(np.float32)
+    if bf16:
+        bits = lambda a: (a.view(np.uint32) >> 16).astype(np.uint16)  # noqa: E731  (truncation is fine here)
+        sv, bv = bits(s32), bits(b32)
+        sf = (sv.astype(np.uint32) << 16).view(np.float32)
+        bf = (bv.astype(np.uint32) << 16).view(np.float32)
+    else:
+        sv, bv = s32.astype(np.float16).view(np.uint16), b32.astype(np.float16).view(np.uint16)
+        sf, bf = sv.view(np.float16).astype(np.float32), bv.view(np.float16).astype(np.float32)
+    x = rng.standard_normal(2048).astype(np.float32)
+    got = O.lm_head(w, sv, bv, x, bf16=bf16)
+    q = np.empty((rows, 2048), np.float64)
+    q[:, 0::2] = w & 0x0F
+    q[:, 1::2] = w >> 4
+    xg = x.astype(np.float64).reshape(32, 64)
+    dots = (q.reshape(rows, 32, 64) * xg[None]).sum(-1)
+    ref = (sf.astype(np.float64) * dots + bf.astype(np.float64) * xg.sum(-1)[None]).sum(-1)
+    assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) < 1e-5

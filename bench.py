@@ -115,6 +115,8 @@ def parse():
     ap.add_argument("--cache-policy", choices=["lru", "slru"], default="lru")
     ap.add_argument("--no-ep", action="store_true",
                     help="skip the expert-parallel block (BASELINE configs[3])")
+    ap.add_argument("--lm-head-only", action="store_true",
+                    help="only the Q4 LM head (248,320 x 2,048, one token); prints its own line")
     ap.add_argument("--ep-only", action="store_true",
                     help="only the expert-parallel block; prints its own line")
     ap.add_argument("--ep-tokens", type=int, default=EP_T)
@@ -604,6 +606,22 @@ def main():
             "timing": "cold cache; CUDA events around the whole stream, end to end through "
                       "qf_moe_stream_step with per-token hidden upload and output read-back",
         }
+
+    if args.lm_head_only:
+        lm = measure_lm_head(args.steps, max(args.warmup, 3))
+        if rank == 0:
+            print(json.dumps({
+                "metric": "Q4 LM-head GB/s (248,320 x 2,048, one fp32 token row)",
+                "value": lm["roofline"]["achieved"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": lm["ms_per_token"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (uniform Q4 codes, fp16 scales |N(0,0.01)|+1e-3, bias -8 scale)",
+                "config": {"workload": lm["workload"]}, "roofline": lm["roofline"],
+                "gpu_launches": args.steps}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     if args.cache_only:
         c = measure_cache_stream(args.cache_tokens, args.cache_slots, args.cache_policy)

@@ -174,6 +174,19 @@ qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
                                const qf_routing *routing, int32_t *idx_out, float *w_out,
                                void *workspace, size_t workspace_bytes);
 
+/* The MoE block from the residual stream: x = post-attention RMSNorm of
+ * `hidden` with weight `norm_w`, then qf_moe_block_forward(x, residual =
+ * hidden).  Replaces the rmsnorm dispatch before the router
+ * (deltanet.metal:18-53 at QwenQ4ActiveExpertStreamingRunner.swift:1169-1176)
+ * together with the MoE step; the norm keeps the reference kernel's order
+ * (64 threads, fma chains, lane butterfly) and rounds x to fp16 for the block.
+ *   hidden: fp32 [T * 2048]; norm_w: fp32 [2048]; workspace: >=
+ *   qf_moe_workspace_size rounded up to 256, plus T * 4096 bytes (x lives at
+ *   its end).  The norm runs as its own 64-thread kernel before the block. */
+qf_status qf_moe_block_forward_prenorm(qf_moe *h, const qf_moe_layer *layer, int32_t T, const float *hidden,
+                                       const float *norm_w, float eps, float *out, const qf_routing *routing,
+                                       int32_t *idx_out, float *w_out, void *workspace, size_t workspace_bytes);
+
 /* n_layers stacked blocks (the decode loop over 40 layers of forwardToken,
  * runner :958).  Layer l reads x_l (fp16) and residual h_l; writes
  * h_{l+1} = out_l; x_{l+1} = fp16(RMSNorm(out_l)) with unit weight and `eps`

@@ -82,6 +82,7 @@ def _declare(L):
     L.qfo_down.argtypes = [_p, _i, _p, _p]
     L.qfo_combine.argtypes = [_p, _p, _p, C.c_float, _p, _p]
     L.qfo_lm_head.argtypes = [_p, _p, _p, _i, _p, _i, _p]
+    L.qfo_post_norm_to_f16.argtypes = [_p, _p, _i, C.c_float, _p]
 
 
 def _ptr(a):
@@ -399,4 +400,14 @@ def lm_head(w: np.ndarray, s: np.ndarray, b: np.ndarray, x: np.ndarray, bf16: bo
     assert w.shape == (rows, 1024) and s.shape == (rows, 32) and b.shape == (rows, 32) and x.shape == (2048,)
     out = np.empty(rows, np.float32)
     lib().qfo_lm_head(_ptr(w), _ptr(s), _ptr(b), rows, _ptr(x), int(bf16), _ptr(out))
+    return out
+
+
+def post_norm_f16(h: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """The post-attention RMSNorm of fp32 rows [T, 2048] with weight w [2048],
+    in qwen_rmsnorm_f32's 64-thread order, as fp16 bits (qfo_post_norm_to_f16)."""
+    h = np.ascontiguousarray(h, np.float32).reshape(-1, HIDDEN)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty(h.shape, np.uint16)
+    lib().qfo_post_norm_to_f16(_ptr(h), _ptr(w), h.shape[0], float(eps), _ptr(out))
     return out

@@ -300,6 +300,26 @@ void qfo_lm_head(const uint8_t *w, const uint16_t *s, const uint16_t *b, int row
         out[r] = qfo_q4_row(w + (size_t)r * 1024, s + (size_t)r * 32, b + (size_t)r * 32, x, 2048, scale_bf16);
 }
 
+/* deltanet.metal:18-53 qwen_rmsnorm_f32 dispatched with 64 threads: thread i
+ * sums v*v over i, i+64, ... (fma chain); simd_sum per 32-lane group (xor
+ * butterfly); the two partials add (simd_sum of [p0, p1, 0, ...]); rsqrt
+ * restated as a correctly rounded 1/sqrt; out = (in * inv) * w, to fp16 */
+void qfo_post_norm_to_f16(const float *in, const float *w, int T, float eps, uint16_t *x_out) {
+    for (int t = 0; t < T; t++) {
+        const float *v = in + (size_t)t * 2048;
+        float lanes[64];
+        for (int i = 0; i < 64; i++) {
+            float acc = 0.0f;
+            for (int j = i; j < 2048; j += 64) acc = fmaf(v[j], v[j], acc);
+            lanes[i] = acc;
+        }
+        const float p0 = butterfly32(lanes), p1 = butterfly32(lanes + 32);
+        const float s = p0 + p1;
+        const float inv = 1.0f / sqrtf(s / 2048.0f + eps);
+        for (int i = 0; i < 2048; i++) x_out[(size_t)t * 2048 + i] = qfo_f32_to_f16((v[i] * inv) * w[i]);
+    }
+}
+
 /* deltanet.metal:2262-2281 qwen_router_q8_logits_simd_f32 */
 void qfo_router_logits(const qfo_layer *L, const float *x, float *logits) {
 #ifdef _OPENMP

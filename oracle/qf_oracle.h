@@ -132,6 +132,9 @@ void qfo_block(const qfo_layer *L, int T, const uint16_t *x, const float *residu
 /* RMSNorm of the stack transition (deltanet.metal:18-53) in a fixed order: 128 tiles of
  * 16 elements, fma chain per tile, tiles summed in order; out = fp16(in * inv) */
 void qfo_rmsnorm_to_f16(const float *in, int T, float eps, uint16_t *x_out);
+/* deltanet.metal:18-53 qwen_rmsnorm_f32 with 64 threads (the post-attention
+ * norm, QwenQ4ActiveExpertStreamingRunner.swift:1169-1176), weighted, then fp16 */
+void qfo_post_norm_to_f16(const float *in, const float *w, int T, float eps, uint16_t *x_out);
 
 /* stable dispatch plan: counts[E], offsets[E+1], perm[T*k] sorted by (expert, token, k) */
 void qfo_dispatch_plan(const int32_t *idx, int T, int k, int E, int32_t *counts,

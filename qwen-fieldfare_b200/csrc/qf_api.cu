@@ -194,6 +194,27 @@ qf_status qf_router_logits_q8(qf_moe* h, const qf_moe_layer* layer, int32_t T, c
   return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_router_logits_q8");
 }
 
+qf_status qf_moe_block_forward_prenorm(qf_moe* h, const qf_moe_layer* layer, int32_t T, const float* hidden,
+                                       const float* norm_w, float eps, float* out, const qf_routing* routing,
+                                       int32_t* idx_out, float* w_out, void* workspace, size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  if (T < 1 || T > qf::kPrefillMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
+  if (!hidden || !norm_w || !out) return fail(h, QF_ERR_ARG, "hidden, norm_w and out are required");
+  size_t need = 0;
+  qf_moe_workspace_size(h, T, &need);
+  need = (need + 255) & ~size_t(255);
+  const size_t x_bytes = (size_t)T * 2048 * 2;
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < need + x_bytes)
+    return fail(h, QF_ERR_ARG, "workspace below qf_moe_workspace_size (rounded to 256) + T * 4096 bytes");
+  uint16_t* x16 = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + need);
+  {
+    DeviceGuard g(h->device);
+    const cudaError_t e = qf::prenorm_f16(stream_of(h), T, hidden, norm_w, eps, x16);
+    if (e != cudaSuccess) return cuda_fail(h, e, "qf_moe_block_forward_prenorm");
+  }
+  return qf_moe_block_forward(h, layer, T, x16, hidden, out, routing, idx_out, w_out, workspace, need);
+}
+
 qf_status qf_lm_head_q4(qf_moe* h, const void* w, const void* scales, const void* biases, int32_t rows,
                         int32_t T, const float* x, float* logits) {
   if (!h) return QF_ERR_ARG;

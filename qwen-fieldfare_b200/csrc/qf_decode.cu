@@ -692,4 +692,38 @@ cudaError_t decode_block(cudaStream_t st, const LayerW& L, bool bf16, int T, con
   return cudaGetLastError();
 }
 
+// Post-attention RMSNorm of the residual stream into the block's fp16 input:
+// deltanet.metal:18-53 qwen_rmsnorm_f32 as dispatched before the router
+// (QwenQ4ActiveExpertStreamingRunner.swift:1169-1176, 64 threads): thread i
+// sums v*v over elements i, i+64, ... with an fma chain, the two 32-lane
+// groups reduce by xor butterfly, the two partials add, mean = sum / 2048,
+// inv = 1 / sqrt(mean + eps) (correctly rounded), x = (h * inv) * w, then fp16.
+// One CTA of 64 threads per token.
+__global__ void __launch_bounds__(64) k_prenorm_f16(const float* __restrict__ h, const float* __restrict__ w,
+                                                    float eps, uint16_t* __restrict__ x16) {
+  __shared__ float partial[2];
+  __shared__ float inv_s;
+  const float* v = h + (size_t)blockIdx.x * kHidden;
+  const int lid = threadIdx.x, lane = lid & 31;
+  float acc = 0.f;
+  for (int i = lid; i < kHidden; i += 64) acc = __fmaf_rn(v[i], v[i], acc);
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  if (lane == 0) partial[lid >> 5] = acc;
+  __syncthreads();
+  if (lid == 0) {
+    const float s = __fadd_rn(partial[0], partial[1]);
+    inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)kHidden), eps)));
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  __half* o = reinterpret_cast<__half*>(x16) + (size_t)blockIdx.x * kHidden;
+  for (int i = lid; i < kHidden; i += 64) o[i] = __float2half_rn(__fmul_rn(__fmul_rn(v[i], inv), w[i]));
+}
+
+cudaError_t prenorm_f16(cudaStream_t st, int T, const float* h, const float* w, float eps, uint16_t* x16) {
+  k_prenorm_f16<<<T, 64, 0, st>>>(h, w, eps, x16);
+  return cudaGetLastError();
+}
+
 }  // namespace qf

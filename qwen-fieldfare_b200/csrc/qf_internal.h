@@ -85,6 +85,9 @@ cudaError_t decode_block(cudaStream_t st, const LayerW& L, bool bf16, int T, con
                          float* w_out, const DecodeWs& ws, uint16_t* x16_next, float eps,
                          int* status, Prof* prof);
 
+// ---- post-attention RMSNorm (qwen_rmsnorm_f32 order) into fp16 block input
+cudaError_t prenorm_f16(cudaStream_t st, int T, const float* h, const float* w, float eps, uint16_t* x16);
+
 // ---- Q4 LM head (qf_lmhead.cu): logits of one fp32 row, rows x 2048 Q4 g64
 cudaError_t lm_head_q4(cudaStream_t st, bool bf16, const void* w, const void* s, const void* b, int rows,
                        const float* x, float* out, int sms);

@@ -136,6 +136,8 @@ SIGNATURES = {
     "qf_store_last_error": (C.c_char_p, []),
     "qf_checkpoint_open": (_S, [C.c_char_p, C.POINTER(_P)]),
     "qf_lm_head_q4": (_S, [_P, _P, _P, _P, _I, _I, _P, _P]),
+    "qf_moe_block_forward_prenorm": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, C.c_float, _P,
+                                          C.POINTER(RoutingDesc), _P, _P, _P, C.c_size_t]),
     "qf_checkpoint_close": (None, [_P]),
     "qf_checkpoint_load_layer": (_S, [_P, _I, C.POINTER(LayerHost), _I, C.POINTER(_I)]),
 }

@@ -234,6 +234,33 @@ def block_forward(ctx: MoEContext, layer: MoELayerWeights, x: torch.Tensor,
     return (out, idx, w) if return_routing else out
 
 
+def block_forward_prenorm(ctx: MoEContext, layer: MoELayerWeights, hidden: torch.Tensor,
+                          norm_w: torch.Tensor, eps: float = 1e-6, *, out: torch.Tensor | None = None,
+                          return_routing: bool = False):
+    """The block from the residual stream: x = fp16(RMSNorm(hidden) * norm_w) in the
+    reference kernel's order, then block_forward(x, residual=hidden)."""
+    if hidden.dtype != torch.float32 or hidden.dim() != 2 or hidden.shape[1] != HIDDEN:
+        raise ValueError("hidden must be float32 [T, 2048]")
+    T = hidden.shape[0]
+    if out is None:
+        out = torch.empty((T, HIDDEN), dtype=torch.float32, device=ctx.device)
+    idx = torch.empty((T, TOPK), dtype=torch.int32, device=ctx.device) if return_routing else None
+    w = torch.empty((T, TOPK), dtype=torch.float32, device=ctx.device) if return_routing else None
+    n = C.c_size_t()
+    check(lib().qf_moe_workspace_size(ctx.h, T, C.byref(n)), ctx.h)
+    need = (n.value + 255) // 256 * 256 + T * HIDDEN * 2
+    ws = ctx._ws.get(("prenorm", T))
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=ctx.device)
+        ctx._ws[("prenorm", T)] = ws
+    ctx._bind_stream()
+    d = layer.desc()
+    check(lib().qf_moe_block_forward_prenorm(ctx.h, C.byref(d), T, _ptr(hidden), _ptr(norm_w), eps,
+                                             _ptr(out), None, _ptr(idx), _ptr(w), _ptr(ws), ws.numel()),
+          ctx.h)
+    return (out, idx, w) if return_routing else out
+
+
 class StackPlan:
     """Host array of layer descriptors for qf_moe_stack_forward."""
 

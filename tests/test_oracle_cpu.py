@@ -206,3 +206,16 @@ def test_lm_head_rows_match_float64(bf16):
     dots = (q.reshape(rows, 32, 64) * xg[None]).sum(-1)
     ref = (sf.astype(np.float64) * dots + bf.astype(np.float64) * xg.sum(-1)[None]).sum(-1)
     assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) < 1e-5
+
+
+def test_post_norm_matches_float64():
+    """qfo_post_norm_to_f16 (qwen_rmsnorm_f32's 64-thread order, weighted) against
+    an fp64 RMSNorm rounded to fp16: at most one fp16 ulp apart."""
+    rng = np.random.default_rng(21)
+    h = (rng.standard_normal((3, 2048)) * 3.0).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(2048)).astype(np.float32)
+    got = O.post_norm_f16(h, w, 1e-6).view(np.float16).astype(np.float64)
+    hd = h.astype(np.float64)
+    ref = (hd / np.sqrt((hd * hd).mean(1, keepdims=True) + 1e-6) * w).astype(np.float16).astype(np.float64)
+    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= ulp)

@@ -182,7 +182,8 @@ qf_status qf_moe_block_forward(qf_moe *h, const qf_moe_layer *layer, int32_t T,
  * (64 threads, fma chains, lane butterfly) and rounds x to fp16 for the block.
  *   hidden: fp32 [T * 2048]; norm_w: fp32 [2048]; workspace: >=
  *   qf_moe_workspace_size rounded up to 256, plus T * 4096 bytes (x lives at
- *   its end).  The norm runs as its own 64-thread kernel before the block. */
+ *   its end).  At T = 1 the norm runs in the one-token kernel's prologue;
+ *   otherwise as a 64-thread kernel before the block. */
 qf_status qf_moe_block_forward_prenorm(qf_moe *h, const qf_moe_layer *layer, int32_t T, const float *hidden,
                                        const float *norm_w, float eps, float *out, const qf_routing *routing,
                                        int32_t *idx_out, float *w_out, void *workspace, size_t workspace_bytes);

@@ -207,6 +207,20 @@ qf_status qf_moe_block_forward_prenorm(qf_moe* h, const qf_moe_layer* layer, int
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < need + x_bytes)
     return fail(h, QF_ERR_ARG, "workspace below qf_moe_workspace_size (rounded to 256) + T * 4096 bytes");
   uint16_t* x16 = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + need);
+  if (T == 1 && h->prof.kernel < 0) {
+    // one token: the norm runs in the one-token kernel's prologue
+    qf::LayerW w;
+    qf_status s = layer_to_w(h, layer, &w);
+    if (s != QF_OK) return s;
+    qf::RoutingArgs r;
+    s = routing_args(h, routing, &r);
+    if (s != QF_OK) return s;
+    DeviceGuard g(h->device);
+    const cudaError_t e = qf::fused1_stack(stream_of(h), &w, 1, h->dims.scale_dtype == QF_SCALE_BF16, nullptr,
+                                           hidden, out, 1e-6f, r, idx_out, w_out, workspace, h->d_status,
+                                           &h->prof, hidden, norm_w, eps);
+    if (e != cudaErrorNotSupported) return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_block_forward_prenorm");
+  }
   {
     DeviceGuard g(h->device);
     const cudaError_t e = qf::prenorm_f16(stream_of(h), T, hidden, norm_w, eps, x16);

@@ -119,6 +119,11 @@ struct Fused1Args {
   int total_layers;  // layers of the whole stack
   const uint16_t* x0;
   const float* res0;
+  // optional: x_0 = fp16(post-attention RMSNorm(pre_h) * pre_w) computed here
+  // (deltanet.metal:18-53 order, 64 threads) instead of read from x0
+  const float* pre_h;
+  const float* pre_w;
+  float pre_eps;
   float* out;
   float eps;
   RoutingArgs r;
@@ -519,7 +524,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
     // ---------------- prologue: x (fp16) and its MMA fragments
     // x_0 is the input; x_l = fp16(h_l / rms(h_l)), the RMS summed over 128 row
     // tiles of 16 rows (fma chain inside a tile, tiles summed in order).
-    if (l == 0) {
+    if (l == 0 && A.pre_h) {
+      // every CTA computes the same norm: threads 0-63 are the reference
+      // kernel's 64 threads (fma chain over i, i + 64, ...), one xor butterfly
+      // per warp, the two partials added, 1 / sqrt correctly rounded
+      float* part = reinterpret_cast<float*>(poll);
+      if (tid < 64) {
+        float acc = 0.f;
+        for (int i = tid; i < kHidden; i += 64) {
+          const float v = __ldg(A.pre_h + i);
+          acc = __fmaf_rn(v, v, acc);
+        }
+#pragma unroll
+        for (int mm = 16; mm >= 1; mm >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, mm));
+        if ((tid & 31) == 0) part[tid >> 5] = acc;
+      }
+      __syncthreads();
+      if (tid == 0)
+        m->inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(__fadd_rn(part[0], part[1]), (float)kHidden),
+                                                       A.pre_eps)));
+      __syncthreads();
+      const float iv = m->inv;
+      const float4 h4 = __ldg(reinterpret_cast<const float4*>(A.pre_h) + tid);
+      const float4 w4 = __ldg(reinterpret_cast<const float4*>(A.pre_w) + tid);
+      reinterpret_cast<__half2*>(xh)[2 * tid] =
+          __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(h4.x, iv), w4.x)),
+                         __float2half_rn(__fmul_rn(__fmul_rn(h4.y, iv), w4.y)));
+      reinterpret_cast<__half2*>(xh)[2 * tid + 1] =
+          __halves2half2(__float2half_rn(__fmul_rn(__fmul_rn(h4.z, iv), w4.z)),
+                         __float2half_rn(__fmul_rn(__fmul_rn(h4.w, iv), w4.w)));
+    } else if (l == 0) {
       if (tid < kHidden / 8) reinterpret_cast<uint4*>(xh)[tid] = reinterpret_cast<const uint4*>(A.x0)[tid];
     } else {
       ll_poll(A.ll_h, kHidden + kNOut, tag - 1u, [&](int i, uint32_t v) { poll[i] = v; }, A.status, &m->fail);
@@ -800,7 +834,7 @@ cudaError_t fused1_init_attributes() {
 cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16,
                          const uint16_t* x, const float* residual, float* out, float eps,
                          const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
-                         int* status, Prof* prof) {
+                         int* status, Prof* prof, const float* pre_h, const float* pre_w, float pre_eps) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -819,7 +853,7 @@ cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bo
   }
   if (g_fused1_grid[dev] < 0) return cudaErrorNotSupported;
   // every bulk copy needs 16-byte aligned sources
-  if (!aligned16(x)) return cudaErrorNotSupported;
+  if (!aligned16(x) || !aligned16(pre_h) || !aligned16(pre_w)) return cudaErrorNotSupported;
   for (int i = 0; i < n_layers; i++) {
     const LayerW& L = layers[i];
     if (!aligned16(L.rw) || !aligned16(L.rs) || !aligned16(L.rb) || !aligned16(L.cw) || !aligned16(L.cs) ||
@@ -836,6 +870,9 @@ cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bo
   A.total_layers = n_layers;
   A.x0 = x;
   A.res0 = residual;
+  A.pre_h = pre_h;
+  A.pre_w = pre_w;
+  A.pre_eps = pre_eps;
   A.out = out;
   A.eps = eps;
   A.r = r;

@@ -114,10 +114,13 @@ cudaError_t fused_stack(cudaStream_t st, const LayerW* layers, int n_layers, boo
 // device has fewer than 128 SMs or a weight pointer is not 16-byte aligned.
 cudaError_t fused1_init_attributes();
 size_t fused1_workspace_bytes();
+// pre_h / pre_w (optional): layer 0's input is the post-attention RMSNorm of
+// pre_h with weight pre_w, computed in the kernel's prologue (x unused)
 cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bool bf16,
                          const uint16_t* x, const float* residual, float* out, float eps,
                          const RoutingArgs& r, int* idx_out, float* w_out, void* workspace,
-                         int* status, Prof* prof);
+                         int* status, Prof* prof, const float* pre_h = nullptr,
+                         const float* pre_w = nullptr, float pre_eps = 0.f);
 
 // ---- prefill path, T > 64 (qf_prefill.cu)
 constexpr int kPrefillMaxTokens = 32768;

@@ -24,6 +24,7 @@
 #include <cerrno>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -32,6 +33,12 @@
 #include <vector>
 
 #include "../../include/qf_moe.h"
+
+namespace qf {
+// qf_sha256_ni.cpp (compiled with the SHA extensions enabled)
+bool sha256_ni_available();
+void sha256_ni_blocks(uint32_t* state, const uint8_t* p, size_t n);
+}  // namespace qf
 
 namespace {
 
@@ -73,10 +80,12 @@ class Sha256 {
       p += take;
       n -= take;
       if (fill_ < sizeof(buf_)) return;
-      block(buf_);
+      blocks(buf_, 1);
       fill_ = 0;
     }
-    for (; n >= 64; p += 64, n -= 64) block(p);
+    blocks(p, n / 64);
+    p += n & ~size_t(63);
+    n &= 63;
     std::memcpy(buf_, p, n);
     fill_ = n;
   }
@@ -100,6 +109,16 @@ class Sha256 {
   }
 
  private:
+  // the SHA extensions when the CPU has them, else the FIPS 180-4 rounds below
+  void blocks(const uint8_t* p, size_t n) {
+    // QF_SHA256_PORTABLE=1 selects the portable rounds (tests compare both)
+    static const bool ni = qf::sha256_ni_available() && !std::getenv("QF_SHA256_PORTABLE");
+    if (ni) {
+      qf::sha256_ni_blocks(h_, p, n);
+      return;
+    }
+    for (; n; n--, p += 64) block(p);
+  }
   static uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
   void block(const uint8_t* p) {
     static const uint32_t k[64] = {

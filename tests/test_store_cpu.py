@@ -238,3 +238,19 @@ def test_open_rejects_damaged_stores(store, tmp_path, damage):
         os.remove(f7)
     with pytest.raises(QfError):
         S.ExpertStore(c)
+
+
+def test_sha256_portable_rounds_match_the_accelerated_ones():
+    """The library hashes with the x86 SHA extensions where the CPU has them;
+    QF_SHA256_PORTABLE=1 selects the FIPS 180-4 rounds.  Both give hashlib's
+    digests (run in a child process: the choice is made once per process)."""
+    import subprocess
+    code = ("import hashlib, numpy as np; from qfmoe import store as S; "
+            "rng = np.random.default_rng(3); "
+            "ok = all(S.sha256_hex(d) == hashlib.sha256(d).hexdigest() for d in "
+            "[rng.integers(0, 256, n, dtype=np.uint8).tobytes() for n in (0, 3, 64, 65, 1000, 1 << 18)]); "
+            "print('ok' if ok else 'bad')")
+    env = dict(os.environ, QF_SHA256_PORTABLE="1",
+               PYTHONPATH=os.path.join(ROOT, "qwen-fieldfare_b200") + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert out.stdout.strip() == "ok", out.stderr

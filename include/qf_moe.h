@@ -358,6 +358,25 @@ qf_status qf_store_get_metrics(const qf_store *s, qf_store_metrics *out);
 /* SHA-256 of one layer's payload against the manifest digest (the builder's
  * layer check, QwenQ4ExpertStoreBuilder.swift:354-370): *matches = 1 or 0. */
 qf_status qf_store_verify_layer(qf_store *s, int32_t layer, int32_t *matches);
+/* QwenQ4ExpertStoreBuilder.pack (QwenQ4ExpertStoreBuilder.swift:59-180):
+ * builds the v2 store of the checkpoint in model_path (out_dir NULL:
+ * <model_path>/qwen_q4_experts) from its switch_mlp tensors.  An existing
+ * store is opened and validated, not rebuilt (layers_written 0).  Progress is
+ * kept in pack.resume.json; a layer is written to <file>.partial, fsynced
+ * and renamed.  A leftover checkpoint, completed or partial file makes the
+ * call fail unless `resume` is set, in which case completed layers are
+ * verified by their payload SHA-256 and the rest are packed.  Records that
+ * read as all zeros stay holes of the pre-sized file (same bytes). */
+typedef struct qf_store_pack_result {
+    int32_t layers_written;
+    uint64_t total_bytes;            /* 40 layer files */
+    char source_index_sha256[65];
+} qf_store_pack_result;
+qf_status qf_store_pack(const char *model_path, const char *out_dir, int32_t resume, qf_store_pack_result *res);
+/* QwenQ4ExpertStoreBuilder.verify (:182-199): opens the store against the
+ * checkpoint's index and checks every layer's header and payload SHA-256. */
+qf_status qf_store_verify(const char *model_path, const char *out_dir, int32_t *layers_verified);
+
 /* ---- MLX checkpoint (safetensors) loader (host) ----------------------- */
 /* The MoE tensors of one layer, read from the checkpoint the reference runs
  * (QwenQ4ActiveExpertStreamingRunner.swift:596-620, names resolved through

@@ -599,6 +599,120 @@ struct qf_checkpoint {
 
 namespace {
 
+bool pwrite_fully(int fd, const void* src, size_t count, uint64_t offset) {
+  size_t done = 0;
+  while (done < count) {
+    const ssize_t r = ::pwrite(fd, static_cast<const uint8_t*>(src) + done, count - done, (off_t)(offset + done));
+    if (r < 0 && errno == EINTR) continue;
+    if (r <= 0) return false;
+    done += (size_t)r;
+  }
+  return true;
+}
+
+qf_status fsync_dir(const std::string& dir) {
+  const int fd = ::open(dir.c_str(), O_RDONLY | O_DIRECTORY | O_CLOEXEC | O_NOFOLLOW);
+  if (fd < 0) return fail(QF_ERR_IO, "open directory failed for " + dir + ": errno " + std::to_string(errno));
+  const int r = ::fsync(fd);
+  ::close(fd);
+  return r == 0 ? QF_OK : fail(QF_ERR_IO, "fsync directory failed for " + dir);
+}
+
+// QwenQ4ExpertStoreBuilder.atomicWrite (:437-473): <path>.tmp, fsync, rename, fsync dir
+qf_status atomic_write(const std::string& text, const std::string& path, const std::string& dir) {
+  const std::string tmp = path + ".tmp";
+  if (::unlink(tmp.c_str()) != 0 && errno != ENOENT) return fail(QF_ERR_IO, "unlink failed for " + tmp);
+  const int fd = ::open(tmp.c_str(), O_WRONLY | O_CREAT | O_EXCL | O_CLOEXEC | O_NOFOLLOW, 0644);
+  if (fd < 0) return fail(QF_ERR_IO, "open failed for " + tmp + ": errno " + std::to_string(errno));
+  const bool ok = pwrite_fully(fd, text.data(), text.size(), 0) && ::fsync(fd) == 0;
+  ::close(fd);
+  if (!ok || ::rename(tmp.c_str(), path.c_str()) != 0) {
+    ::unlink(tmp.c_str());
+    return fail(QF_ERR_IO, "write failed for " + path);
+  }
+  return fsync_dir(dir);
+}
+
+qf_status mkdirs(const std::string& path) {
+  std::string cur;
+  size_t i = 0;
+  while (i <= path.size()) {
+    const size_t j = path.find('/', i);
+    cur = path.substr(0, j == std::string::npos ? path.size() : j);
+    if (!cur.empty() && ::mkdir(cur.c_str(), 0755) != 0 && errno != EEXIST)
+      return fail(QF_ERR_IO, "mkdir failed for " + cur + ": errno " + std::to_string(errno));
+    if (j == std::string::npos) break;
+    i = j + 1;
+  }
+  return QF_OK;
+}
+
+// JSON as the builder's encoder writes it (pretty-printed, keys sorted)
+std::string json_layer(const LayerEntry& e, const char* indent) {
+  const std::string in(indent);
+  return in + "{\n" + in + "  \"fileSize\" : " + std::to_string(e.file_size) + ",\n" + in + "  \"filename\" : \"" +
+         e.filename + "\",\n" + in + "  \"layerIndex\" : " + std::to_string(e.layer_index) + ",\n" + in +
+         "  \"payloadSHA256\" : \"" + e.payload_sha256 + "\"\n" + in + "}";
+}
+std::string json_layers(const std::vector<LayerEntry>& ls) {
+  if (ls.empty()) return "[\n\n  ]";
+  std::string o = "[\n";
+  for (size_t i = 0; i < ls.size(); i++) o += json_layer(ls[i], "    ") + (i + 1 < ls.size() ? ",\n" : "\n");
+  return o + "  ]";
+}
+std::string manifest_json(const std::string& src, const std::vector<LayerEntry>& ls) {
+  return "{\n  \"layers\" : " + json_layers(ls) + ",\n  \"schemaVersion\" : 2,\n  \"sourceIndexSHA256\" : \"" + src +
+         "\"\n}";
+}
+std::string resume_json(const std::string& src, const std::vector<LayerEntry>& ls) {
+  return "{\n  \"completedLayers\" : " + json_layers(ls) + ",\n  \"schemaVersion\" : 2,\n  \"sourceIndexSHA256\" : \"" +
+         src + "\"\n}";
+}
+
+bool file_exists(const std::string& p) {
+  struct stat st;
+  return ::lstat(p.c_str(), &st) == 0;
+}
+
+// QwenQ4ExpertStoreBuilder.verifyLayerFile (:373-401)
+qf_status verify_layer_file(const std::string& path, const LayerEntry& expected, const std::string& src) {
+  const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC | O_NOFOLLOW);
+  if (fd < 0) return fail(QF_ERR_IO, "open failed for " + path + ": errno " + std::to_string(errno));
+  struct stat info;
+  if (::fstat(fd, &info) != 0 || (int64_t)info.st_size != expected.file_size) {
+    ::close(fd);
+    return fail(QF_ERR_ARG, "invalid header: file size mismatch for " + path);
+  }
+  uint8_t hb[kHeaderBytes];
+  qf_store_header h;
+  if (pread_fully(fd, hb, kHeaderBytes, 0) != kHeaderBytes) {
+    ::close(fd);
+    return fail(QF_ERR_IO, "short read from " + path);
+  }
+  qf_status st = qf_store_header_decode(hb, kHeaderBytes, &h);
+  if (st == QF_OK && (h.layer_index != expected.layer_index || h.experts_per_layer != kExpertsPerLayer ||
+                      (uint64_t)h.expert_byte_length != kRecordBytes || h.payload_byte_length != kPayloadBytes ||
+                      std::string(h.payload_sha256, 64) != expected.payload_sha256 ||
+                      std::string(h.source_index_sha256, 64) != src))
+    st = fail(QF_ERR_ARG, "invalid header: metadata mismatch for " + path);
+  if (st == QF_OK) {
+    Sha256 hs;
+    std::vector<uint8_t> buf(1u << 20);
+    uint64_t off = kHeaderBytes, left = kPayloadBytes;
+    while (left && st == QF_OK) {
+      const size_t want = (size_t)std::min<uint64_t>(left, buf.size());
+      if (pread_fully(fd, buf.data(), want, off) != want) st = fail(QF_ERR_IO, "short read from " + path);
+      hs.update(buf.data(), want);
+      off += want;
+      left -= want;
+    }
+    if (st == QF_OK && hs.hex() != expected.payload_sha256)
+      st = fail(QF_ERR_ARG, "invalid header: payload SHA-256 mismatch for " + path);
+  }
+  ::close(fd);
+  return st;
+}
+
 qf_status read_slice(const Slice& sl, uint64_t at, void* dst, uint64_t n, const std::string& name) {
   if (pread_fully(sl.fd, dst, n, sl.offset + at) != n) return fail(QF_ERR_IO, "short read of " + name);
   return QF_OK;
@@ -934,6 +1048,220 @@ qf_status qf_checkpoint_load_layer(qf_checkpoint* c, int32_t layer, const qf_lay
       return fail(QF_ERR_IO, "short read of " + swname[bad.load() % 9] + " expert " + std::to_string(bad.load() / 9));
   }
   if (scale_dtype) *scale_dtype = dtype16 == "BF16" ? QF_SCALE_BF16 : QF_SCALE_F16;
+  return QF_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// QwenQ4ExpertStoreBuilder.packLayer (:284-352): the layer's 256 records
+// from the checkpoint slices into <final>.partial, digest, header, fsync,
+// rename.  Records that read as all zeros are left as holes of the
+// pre-sized file (same bytes, no write).
+qf_status pack_layer(int layer, const Slice* sl, const std::string& src, const std::string& dir,
+                     const std::string& partial, const std::string& final_path, LayerEntry& entry) {
+  const int fd = ::open(partial.c_str(), O_RDWR | O_CREAT | O_EXCL | O_CLOEXEC | O_NOFOLLOW, 0644);
+  if (fd < 0) return fail(QF_ERR_IO, "open failed for " + partial + ": errno " + std::to_string(errno));
+  qf_status st = QF_OK;
+  if (::ftruncate(fd, (off_t)kLayerFileBytes) != 0) st = fail(QF_ERR_IO, "ftruncate failed for " + partial);
+  std::vector<uint64_t> rec64(kRecordBytes / 8);
+  uint8_t* rec = reinterpret_cast<uint8_t*>(rec64.data());
+  Sha256 h;
+  for (int e = 0; e < kExpertsPerLayer && st == QF_OK; e++) {
+    for (int k = 0; k < 9 && st == QF_OK; k++)
+      if (pread_fully(sl[k].fd, rec + kComponentOffset[k], kComponentBytes[k],
+                      sl[k].offset + (uint64_t)e * kComponentBytes[k]) != kComponentBytes[k])
+        st = fail(QF_ERR_IO, "short read of layer " + std::to_string(layer) + " expert " + std::to_string(e));
+    if (st != QF_OK) break;
+    h.update(rec, kRecordBytes);
+    bool zero = true;
+    for (uint64_t w : rec64)
+      if (w) {
+        zero = false;
+        break;
+      }
+    if (!zero && !pwrite_fully(fd, rec, kRecordBytes, kHeaderBytes + (uint64_t)e * kRecordBytes))
+      st = fail(QF_ERR_IO, "pwrite failed for " + partial);
+  }
+  if (st == QF_OK) {
+    qf_store_header hd;
+    std::memset(&hd, 0, sizeof hd);
+    hd.layer_index = layer;
+    hd.experts_per_layer = kExpertsPerLayer;
+    hd.expert_byte_length = (int32_t)kRecordBytes;
+    hd.payload_byte_length = kPayloadBytes;
+    const std::string digest = h.hex();
+    std::memcpy(hd.payload_sha256, digest.c_str(), 65);
+    std::memcpy(hd.source_index_sha256, src.c_str(), 65);
+    uint8_t hb[kHeaderBytes];
+    st = qf_store_header_encode(&hd, hb);
+    if (st == QF_OK && !pwrite_fully(fd, hb, kHeaderBytes, 0)) st = fail(QF_ERR_IO, "pwrite failed for " + partial);
+    if (st == QF_OK && ::fsync(fd) != 0) st = fail(QF_ERR_IO, "fsync failed for " + partial);
+    entry.layer_index = layer;
+    entry.filename = layer_filename(layer);
+    entry.file_size = (int64_t)kLayerFileBytes;
+    entry.payload_sha256 = digest;
+  }
+  ::close(fd);
+  if (st == QF_OK && ::rename(partial.c_str(), final_path.c_str()) != 0)
+    st = fail(QF_ERR_IO, "rename failed for " + partial);
+  if (st == QF_OK) st = fsync_dir(dir);
+  return st;
+}
+
+qf_status write_resume(const std::string& path, const std::string& dir, const std::string& src,
+                       const std::map<int64_t, LayerEntry>& done) {
+  std::vector<LayerEntry> ls;
+  for (auto& kv : done) ls.push_back(kv.second);
+  return atomic_write(resume_json(src, ls), path, dir);
+}
+
+}  // namespace
+
+extern "C" {
+
+qf_status qf_store_pack(const char* model_path, const char* out_dir, int32_t resume, qf_store_pack_result* res) {
+  if (!model_path) return fail(QF_ERR_ARG, "qf_store_pack: null model path");
+  const std::string model = model_path;
+  const std::string out = out_dir ? std::string(out_dir) : model + "/qwen_q4_experts";
+  const std::string index = model + "/model.safetensors.index.json";
+  std::string src;
+  if (!hash_file(index, src)) return fail(QF_ERR_IO, "open failed for " + index);
+  auto report = [&](int written) {
+    if (res) {
+      res->layers_written = written;
+      res->total_bytes = (uint64_t)kLayers * kLayerFileBytes;
+      std::memcpy(res->source_index_sha256, src.c_str(), 65);
+    }
+    return QF_OK;
+  };
+  // an existing store is opened (and so validated), not rebuilt
+  if (file_exists(out + "/manifest.json")) {
+    qf_store* st = nullptr;
+    const qf_status s = qf_store_open(out.c_str(), index.c_str(), &st);
+    if (s != QF_OK) return s;
+    qf_store_close(st);
+    return report(0);
+  }
+  qf_status st = mkdirs(out);
+  if (st != QF_OK) return st;
+  const std::string ck = out + "/pack.resume.json";
+  std::map<int64_t, LayerEntry> done;
+  if (file_exists(ck)) {
+    if (!resume) return fail(QF_ERR_ARG, "partial store: use resume to continue " + ck);
+    std::string text;
+    Json root;
+    if (!read_file(ck, text) || !JsonParser(text.data(), text.size()).parse(root) || root.kind != Json::Obj)
+      return fail(QF_ERR_ARG, "partial store: unreadable " + ck);
+    int64_t schema = 0;
+    std::string csrc;
+    auto cl = root.obj.find("completedLayers");
+    if (!get_int(root, "schemaVersion", schema) || !get_str(root, "sourceIndexSHA256", csrc) ||
+        cl == root.obj.end() || cl->second.kind != Json::Arr || schema != (int64_t)kSchema || csrc != src)
+      return fail(QF_ERR_ARG, "partial store: checkpoint does not match this source model");
+    for (const Json& e : cl->second.arr) {
+      LayerEntry le;
+      if (e.kind != Json::Obj || !get_int(e, "layerIndex", le.layer_index) || !get_str(e, "filename", le.filename) ||
+          !get_int(e, "fileSize", le.file_size) || !get_str(e, "payloadSHA256", le.payload_sha256) ||
+          le.layer_index < 0 || le.layer_index >= kLayers)
+        return fail(QF_ERR_ARG, "partial store: malformed completed layer in " + ck);
+      done[le.layer_index] = le;
+    }
+  } else {
+    st = write_resume(ck, out, src, done);
+    if (st != QF_OK) return st;
+  }
+  qf_checkpoint* cp = nullptr;
+  st = qf_checkpoint_open(model_path, &cp);
+  if (st != QF_OK) return st;
+  std::unique_ptr<qf_checkpoint> guard(cp);
+  std::vector<Slice> sl((size_t)kLayers * 9);
+  for (int l = 0; l < kLayers; l++)
+    for (int k = 0; k < 9; k++) {
+      const std::string name = "language_model.model.layers." + std::to_string(l) + ".mlp.switch_mlp." +
+                               kComponentSuffix[k];
+      st = cp->find(name, sl[(size_t)l * 9 + k]);
+      if (st != QF_OK) return st;
+      if (sl[(size_t)l * 9 + k].bytes != kComponentBytes[k] * kExpertsPerLayer)
+        return fail(QF_ERR_ARG, "invalid manifest: unexpected byte length for " + name);
+    }
+  int written = 0;
+  for (int l = 0; l < kLayers; l++) {
+    const std::string fname = layer_filename(l), final_path = out + "/" + fname, partial = final_path + ".partial";
+    auto it = done.find(l);
+    if (it != done.end()) {
+      st = verify_layer_file(final_path, it->second, src);
+      if (st != QF_OK) return st;
+      continue;
+    }
+    if (file_exists(final_path)) {
+      if (!resume) return fail(QF_ERR_ARG, "partial store: unexpected completed file " + final_path + "; use resume");
+      const int fd = ::open(final_path.c_str(), O_RDONLY | O_CLOEXEC | O_NOFOLLOW);
+      uint8_t hb[kHeaderBytes];
+      const bool got = fd >= 0 && pread_fully(fd, hb, kHeaderBytes, 0) == kHeaderBytes;
+      if (fd >= 0) ::close(fd);
+      if (!got) return fail(QF_ERR_IO, "short read from " + final_path);
+      qf_store_header h;
+      st = qf_store_header_decode(hb, kHeaderBytes, &h);
+      if (st != QF_OK) return st;
+      LayerEntry le;
+      le.layer_index = l;
+      le.filename = fname;
+      le.file_size = (int64_t)kLayerFileBytes;
+      le.payload_sha256 = std::string(h.payload_sha256, 64);
+      st = verify_layer_file(final_path, le, src);
+      if (st == QF_OK) {
+        done[l] = le;
+        st = write_resume(ck, out, src, done);
+      }
+      if (st != QF_OK) return st;
+      continue;
+    }
+    if (file_exists(partial)) {
+      if (!resume) return fail(QF_ERR_ARG, "partial store: unfinished layer file " + partial + "; use resume");
+      if (::unlink(partial.c_str()) != 0) return fail(QF_ERR_IO, "unlink failed for " + partial);
+      st = fsync_dir(out);
+      if (st != QF_OK) return st;
+    }
+    LayerEntry le;
+    st = pack_layer(l, &sl[(size_t)l * 9], src, out, partial, final_path, le);
+    if (st == QF_OK) {
+      done[l] = le;
+      st = write_resume(ck, out, src, done);
+    }
+    if (st != QF_OK) return st;
+    written++;
+  }
+  std::vector<LayerEntry> ls;
+  for (auto& kv : done) ls.push_back(kv.second);
+  const std::string text = manifest_json(src, ls);
+  Manifest m;
+  st = parse_manifest(text.data(), text.size(), m);
+  if (st == QF_OK) st = atomic_write(text, out + "/manifest.json", out);
+  if (st != QF_OK) return st;
+  if (::unlink(ck.c_str()) != 0 && errno != ENOENT) return fail(QF_ERR_IO, "unlink failed for " + ck);
+  st = fsync_dir(out);
+  return st == QF_OK ? report(written) : st;
+}
+
+qf_status qf_store_verify(const char* model_path, const char* out_dir, int32_t* layers_verified) {
+  if (!model_path) return fail(QF_ERR_ARG, "qf_store_verify: null model path");
+  const std::string model = model_path;
+  const std::string out = out_dir ? std::string(out_dir) : model + "/qwen_q4_experts";
+  const std::string index = model + "/model.safetensors.index.json";
+  qf_store* s = nullptr;
+  qf_status st = qf_store_open(out.c_str(), index.c_str(), &s);
+  if (st != QF_OK) return st;
+  std::unique_ptr<qf_store> guard(s);
+  int n = 0;
+  for (int l = 0; l < kLayers; l++) {
+    const LayerEntry& le = s->manifest.layers[l];
+    st = verify_layer_file(out + "/" + le.filename, le, s->manifest.source_index_sha256);
+    if (st != QF_OK) return st;
+    n++;
+  }
+  if (layers_verified) *layers_verified = n;
   return QF_OK;
 }
 

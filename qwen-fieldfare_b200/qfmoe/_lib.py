@@ -68,6 +68,11 @@ class LayerHost(C.Structure):
                [("record_stride", C.c_uint64)]
 
 
+class StorePackResult(C.Structure):
+    _fields_ = [("layers_written", C.c_int32), ("total_bytes", C.c_uint64),
+                ("source_index_sha256", C.c_char * 65)]
+
+
 # (name, restype, argtypes) for every symbol include/qf_moe.h declares.
 _P = C.c_void_p
 _I = C.c_int32
@@ -135,6 +140,8 @@ SIGNATURES = {
     "qf_sha256_hex": (_S, [_P, C.c_size_t, _P]),
     "qf_store_last_error": (C.c_char_p, []),
     "qf_checkpoint_open": (_S, [C.c_char_p, C.POINTER(_P)]),
+    "qf_store_pack": (_S, [C.c_char_p, C.c_char_p, _I, C.POINTER(StorePackResult)]),
+    "qf_store_verify": (_S, [C.c_char_p, C.c_char_p, C.POINTER(_I)]),
     "qf_lm_head_q4": (_S, [_P, _P, _P, _P, _I, _I, _P, _P]),
     "qf_moe_block_forward_prenorm": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, C.c_float, _P,
                                           C.POINTER(RoutingDesc), _P, _P, _P, C.c_size_t]),

@@ -196,3 +196,21 @@ class Checkpoint:
         return MoELayerWeights(up(host["router_w"]), up(host["router_s"], True), up(host["router_b"], True),
                                up(host["coef_w"]), up(host["coef_s"], True), up(host["coef_b"], True),
                                up(host["shared"]), up(host["bank"])), dtype
+
+
+def pack_store(model_path: str, out_dir: str | None = None, resume: bool = False) -> dict:
+    """Build the v2 store from the checkpoint's switch_mlp tensors
+    (QwenQ4ExpertStoreBuilder.pack; qf_store_pack)."""
+    from ._lib import StorePackResult
+    r = StorePackResult()
+    _ok(lib().qf_store_pack(os.fsencode(model_path), os.fsencode(out_dir) if out_dir else None, int(resume),
+                            C.byref(r)))
+    return {"layers_written": r.layers_written, "total_bytes": r.total_bytes,
+            "source_index_sha256": r.source_index_sha256.decode()}
+
+
+def verify_store(model_path: str, out_dir: str | None = None) -> int:
+    """Every layer's header and payload SHA-256 (QwenQ4ExpertStoreBuilder.verify)."""
+    n = C.c_int32()
+    _ok(lib().qf_store_verify(os.fsencode(model_path), os.fsencode(out_dir) if out_dir else None, C.byref(n)))
+    return n.value

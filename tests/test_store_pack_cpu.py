@@ -111,3 +111,23 @@ def test_a_changed_source_index_is_refused(packed, tmp_path):
         S.pack_store(c)
     with pytest.raises(QfError, match="source mismatch"):
         S.verify_store(c)
+
+
+def test_pack_refuses_a_checkpoint_without_every_expert_tensor(tmp_path):
+    """Discovery fails before any layer is written (the builder's
+    discoverSlices: every layer's nine switch_mlp tensors must exist)."""
+    d = str(tmp_path / "ck")
+    tensors = {}
+    for layer in range(40):
+        pre = f"language_model.model.layers.{layer}.mlp.switch_mlp."
+        for suffix, n, shape, is16 in O.COMPONENTS:
+            if layer == 17 and suffix == "down_proj.biases":
+                continue
+            tensors[pre + suffix] = ("F16" if is16 else "U32", (256,) + shape, O.Sparse(256 * n, {}))
+    O.write_checkpoint(d, tensors, n_shards=2)
+    with pytest.raises(QfError, match="layers.17.mlp.switch_mlp.down_proj.biases"):
+        S.pack_store(d)
+    out = os.path.join(d, "qwen_q4_experts")
+    assert not any(name.endswith(".q4exp") for name in os.listdir(out))
+    with pytest.raises(QfError, match="resume"):  # the progress file it left behind
+        S.pack_store(d)

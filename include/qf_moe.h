@@ -389,7 +389,8 @@ qf_status qf_store_verify(const char *model_path, const char *out_dir, int32_t *
  *   mlp.switch_mlp.{gate,up,down}_proj.*          -> expert_bank (256 records)
  * Tensor byte lengths are checked (as the builder does); scales and biases
  * must all be BF16 or all F16, reported through *scale_dtype.  Any dst
- * pointer may be NULL to skip that part. */
+ * pointer may be NULL to skip that part.  Shard headers are parsed on first
+ * use, so one qf_checkpoint is used by one thread at a time. */
 typedef struct qf_checkpoint qf_checkpoint;
 typedef struct qf_layer_host {
     void *router_w;       /* 524,288 bytes: Q8 codes [256][2048] */

@@ -59,22 +59,29 @@ cudaStream_t stream_of(const qf_moe* h) { return h->stream; }
 
 }  // namespace
 
-qf_status qf::layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
-  if (!l) return fail(h, QF_ERR_ARG, "layer descriptor is NULL");
+qf_status qf::check_layer(const qf_moe_layer* l, qf::LayerW* w, const char** why) {
+  auto bad = [&](const char* m) {
+    if (why) *why = m;
+    return QF_ERR_ARG;
+  };
+  if (!l) return bad("layer descriptor is NULL");
   if (!l->router_w || !l->router_s || !l->router_b || !l->coef_w || !l->coef_s || !l->coef_b ||
       !l->shared_record || !l->expert_bank)
-    return fail(h, QF_ERR_ARG, "layer descriptor has a NULL weight pointer");
+    return bad("layer descriptor has a NULL weight pointer");
   if (l->record_stride < qf::kRecordBytes || (l->record_stride % 32) != 0)
-    return fail(h, QF_ERR_ARG, "record_stride must be >= 1769472 and a multiple of 32");
+    return bad("record_stride must be >= 1769472 and a multiple of 32");
+  // the router and coefficient codes are read as uint4, their scales/biases as
+  // 16-bit words (router rows 16 bytes at a time)
   if (!aligned(l->router_w, 16) || !aligned(l->coef_w, 16) || !aligned(l->router_s, 16) ||
       !aligned(l->router_b, 16) || !aligned(l->coef_s, 2) || !aligned(l->coef_b, 2))
-    return fail(h, QF_ERR_ARG, "router codes/scales/biases must be 16-byte aligned");
+    return bad("router/coefficient codes and router scales/biases must be 16-byte aligned, "
+               "coefficient scales/biases 2-byte aligned");
   // expert codes are read 32 bytes at a time
   if (!aligned(l->shared_record, 32) || !aligned(l->expert_bank, 32))
-    return fail(h, QF_ERR_ARG, "shared record and bank must be 32-byte aligned");
+    return bad("shared record and bank must be 32-byte aligned");
   if (l->bank_records == 0 || l->bank_records >= (1u << 23))
-    return fail(h, QF_ERR_ARG, "bank_records must be in [1, 2^23)");
-  if (l->reserved != 0) return fail(h, QF_ERR_ARG, "reserved field must be 0");
+    return bad("bank_records must be in [1, 2^23)");
+  if (l->reserved != 0) return bad("reserved field must be 0");
   w->rw = l->router_w;
   w->rs = l->router_s;
   w->rb = l->router_b;
@@ -86,6 +93,12 @@ qf_status qf::layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
   w->stride = l->record_stride;
   w->bank_records = l->bank_records;
   return QF_OK;
+}
+
+qf_status qf::layer_to_w(qf_moe* h, const qf_moe_layer* l, qf::LayerW* w) {
+  const char* why = "";
+  qf_status s = check_layer(l, w, &why);
+  return s == QF_OK ? QF_OK : fail(h, s, "%s", why);
 }
 
 namespace {

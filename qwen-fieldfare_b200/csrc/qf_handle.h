@@ -22,6 +22,10 @@ namespace qf {
 // Sets the handle's error text (printf-style with one string argument).
 qf_status fail(qf_moe* h, qf_status s, const char* fmt, const char* a = "");
 qf_status cuda_fail(qf_moe* h, cudaError_t e, const char* where);
-// Checks one layer descriptor and converts it for the kernels.
+// Checks one layer descriptor (pointers, alignment, stride, bank size) and
+// converts it for the kernels; on failure *why names the broken rule.  Needs
+// no handle: the allocation-free entry applies the same rules.
+qf_status check_layer(const qf_moe_layer* l, LayerW* w, const char** why);
+// check_layer with the failure text stored in the handle.
 qf_status layer_to_w(qf_moe* h, const qf_moe_layer* l, LayerW* w);
 }  // namespace qf

@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "../../include/qf_moe.h"
+#include "qf_handle.h"
 #include "qf_internal.h"
 
 namespace qf {
@@ -65,16 +66,11 @@ extern "C" qf_status qf_moe_block_forward_static(int32_t scale_dtype, const qf_m
                                                  int32_t* idx_out, float* w_out, void* stream) {
   if (T < 1 || T > qf::kStaticMaxTokens) return QF_ERR_ARG;
   if (scale_dtype != QF_SCALE_F16 && scale_dtype != QF_SCALE_BF16) return QF_ERR_ARG;
-  if (!layer || !x || !out || (reinterpret_cast<uintptr_t>(x) % 16) != 0) return QF_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(layer->router_w) | reinterpret_cast<uintptr_t>(layer->router_s) |
-       reinterpret_cast<uintptr_t>(layer->router_b) | reinterpret_cast<uintptr_t>(layer->shared_record) |
-       reinterpret_cast<uintptr_t>(layer->expert_bank)) % 16 != 0)
-    return QF_ERR_ARG;
-  if (!layer->router_w || !layer->router_s || !layer->router_b || !layer->coef_w ||
-      !layer->coef_s || !layer->coef_b || !layer->shared_record || !layer->expert_bank ||
-      layer->record_stride < qf::kRecordBytes || (layer->record_stride % 16) != 0 ||
-      layer->bank_records == 0 || layer->bank_records >= (1u << 23) || layer->reserved != 0)
-    return QF_ERR_ARG;
+  if (!x || !out || (reinterpret_cast<uintptr_t>(x) % 16) != 0) return QF_ERR_ARG;
+  // the same descriptor rules as qf_moe_block_forward: a descriptor rejected
+  // there is rejected here, before anything is launched
+  qf::LayerW w;
+  if (qf::check_layer(layer, &w, nullptr) != QF_OK) return QF_ERR_ARG;
   if (qf::decode_workspace_bytes(T) + qf::kStaticStatusBytes > qf::kStaticScratchBytes)
     return QF_ERR_ARG;
   int dev = -1;
@@ -87,17 +83,6 @@ extern "C" qf_status qf_moe_block_forward_static(int32_t scale_dtype, const qf_m
   if (cudaMemsetAsync(status, 0, qf::kStaticStatusBytes, st) != cudaSuccess) return QF_ERR_CUDA;
   qf::DecodeWs ws;
   qf::decode_carve(static_cast<unsigned char*>(base) + qf::kStaticStatusBytes, T, &ws);
-  qf::LayerW w;
-  w.rw = layer->router_w;
-  w.rs = layer->router_s;
-  w.rb = layer->router_b;
-  w.cw = layer->coef_w;
-  w.cs = layer->coef_s;
-  w.cb = layer->coef_b;
-  w.shared = layer->shared_record;
-  w.bank = layer->expert_bank;
-  w.stride = layer->record_stride;
-  w.bank_records = layer->bank_records;
   qf::RoutingArgs r = {nullptr, nullptr, nullptr, nullptr};
   cudaError_t e = qf::decode_block(st, w, scale_dtype == QF_SCALE_BF16, T, x, residual, out, r,
                                    idx_out, w_out, ws, nullptr, 0.f, status, nullptr);

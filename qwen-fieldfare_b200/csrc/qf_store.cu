@@ -554,6 +554,37 @@ struct qf_checkpoint {
     for (auto& kv : shards)
       if (kv.second.fd >= 0) ::close(kv.second.fd);
   }
+  // The safetensors header of one shard: u64 length, then JSON whose tensors
+  // carry data_offsets relative to the end of the header.
+  qf_status parse_shard_header(int fd, const std::string& file, const std::string& path,
+                               std::map<std::string, Slice>& tensors) {
+    uint8_t lb[8];
+    if (pread_fully(fd, lb, 8, 0) != 8) return fail(QF_ERR_IO, "short read from " + path);
+    const uint64_t hlen = get64(lb);
+    if (hlen == 0 || hlen > (256ull << 20))
+      return fail(QF_ERR_ARG, "invalid manifest: invalid safetensors header length in " + file);
+    std::string text(hlen, '\0');
+    if (pread_fully(fd, &text[0], hlen, 8) != hlen) return fail(QF_ERR_IO, "short read from " + path);
+    Json root;
+    if (!JsonParser(text.data(), text.size()).parse(root) || root.kind != Json::Obj)
+      return fail(QF_ERR_ARG, "invalid manifest: invalid safetensors header in " + file);
+    for (auto& kv : root.obj) {
+      if (kv.first == "__metadata__" || kv.second.kind != Json::Obj) continue;
+      auto off = kv.second.obj.find("data_offsets");
+      if (off == kv.second.obj.end() || off->second.kind != Json::Arr || off->second.arr.size() != 2 ||
+          !off->second.arr[0].integral || !off->second.arr[1].integral)
+        continue;
+      const int64_t b = off->second.arr[0].i, e = off->second.arr[1].i;
+      if (b < 0 || e < b) continue;
+      Slice sl;
+      sl.fd = fd;
+      sl.offset = 8 + hlen + (uint64_t)b;
+      sl.bytes = (uint64_t)(e - b);
+      get_str(kv.second, "dtype", sl.dtype);
+      tensors[kv.first] = sl;
+    }
+    return QF_OK;
+  }
   // the tensor's slice; QwenQ4ExpertStoreBuilder.discoverSlices (:202-282)
   qf_status find(const std::string& name, Slice& out) {
     auto w = weight_map.find(name);
@@ -561,33 +592,18 @@ struct qf_checkpoint {
     Shard& sh = shards[w->second];
     if (!sh.parsed) {
       sh.path = dir + "/" + w->second;
-      sh.fd = ::open(sh.path.c_str(), O_RDONLY | O_CLOEXEC | O_NOFOLLOW);
-      if (sh.fd < 0) return fail(QF_ERR_IO, "open failed for " + sh.path + ": errno " + std::to_string(errno));
-      uint8_t lb[8];
-      if (pread_fully(sh.fd, lb, 8, 0) != 8) return fail(QF_ERR_IO, "short read from " + sh.path);
-      const uint64_t hlen = get64(lb);
-      if (hlen == 0 || hlen > (256ull << 20))
-        return fail(QF_ERR_ARG, "invalid manifest: invalid safetensors header length in " + w->second);
-      std::string text(hlen, '\0');
-      if (pread_fully(sh.fd, &text[0], hlen, 8) != hlen) return fail(QF_ERR_IO, "short read from " + sh.path);
-      Json root;
-      if (!JsonParser(text.data(), text.size()).parse(root) || root.kind != Json::Obj)
-        return fail(QF_ERR_ARG, "invalid manifest: invalid safetensors header in " + w->second);
-      for (auto& kv : root.obj) {
-        if (kv.first == "__metadata__" || kv.second.kind != Json::Obj) continue;
-        auto off = kv.second.obj.find("data_offsets");
-        if (off == kv.second.obj.end() || off->second.kind != Json::Arr || off->second.arr.size() != 2 ||
-            !off->second.arr[0].integral || !off->second.arr[1].integral)
-          continue;
-        const int64_t b = off->second.arr[0].i, e = off->second.arr[1].i;
-        if (b < 0 || e < b) continue;
-        Slice sl;
-        sl.fd = sh.fd;
-        sl.offset = 8 + hlen + (uint64_t)b;
-        sl.bytes = (uint64_t)(e - b);
-        get_str(kv.second, "dtype", sl.dtype);
-        sh.tensors[kv.first] = sl;
+      // the shard's descriptor is kept only once its header parsed; every
+      // failure closes it, so a later find on the same shard opens afresh
+      const int fd = ::open(sh.path.c_str(), O_RDONLY | O_CLOEXEC | O_NOFOLLOW);
+      if (fd < 0) return fail(QF_ERR_IO, "open failed for " + sh.path + ": errno " + std::to_string(errno));
+      std::map<std::string, Slice> tensors;
+      const qf_status ps = parse_shard_header(fd, w->second, sh.path, tensors);
+      if (ps != QF_OK) {
+        ::close(fd);
+        return ps;
       }
+      sh.fd = fd;
+      sh.tensors.swap(tensors);
       sh.parsed = true;
     }
     auto t = sh.tensors.find(name);

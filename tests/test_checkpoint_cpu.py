@@ -139,3 +139,30 @@ def test_bad_index_and_missing_shard(ckpt, tmp_path):
             c.load_layer(17)
     with pytest.raises(QfError, match="QF_ERR_IO"):
         Checkpoint(str(tmp_path / "nowhere"))
+
+
+def _open_fds():
+    return len(os.listdir("/proc/self/fd"))
+
+
+def test_bad_shard_header_leaks_no_descriptor(ckpt, tmp_path):
+    """A shard whose safetensors header does not parse fails every load with
+    QF_ERR_ARG, and each failed open is closed: repeated loads keep the
+    process's descriptor count unchanged."""
+    d, _ = ckpt
+    some = json.load(open(os.path.join(d, "model.safetensors.index.json")))["weight_map"]
+    shard = sorted(set(some.values()))[0]
+
+    def corrupt(idx, dst):
+        with open(os.path.join(dst, shard), "wb") as f:
+            f.write((16).to_bytes(8, "little") + b"not a json head!")
+
+    _rewrite(d, str(tmp_path / "c"), corrupt)
+    with Checkpoint(str(tmp_path / "c")) as c:
+        with pytest.raises(QfError, match="safetensors header"):
+            c.load_layer(17)
+        n0 = _open_fds()
+        for _ in range(5):
+            with pytest.raises(QfError, match="safetensors header"):
+                c.load_layer(17)
+        assert _open_fds() == n0

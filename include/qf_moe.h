@@ -267,6 +267,12 @@ qf_status qf_cache_reset_metrics(qf_cache *c);
 qf_status qf_cache_get_metrics(const qf_cache *c, qf_cache_metrics_t *out);
 qf_status qf_cache_info(const qf_cache *c, int32_t *layer_count,
                         int32_t *probationary_capacity, int32_t *protected_capacity);
+/* Per-layer demand counters since the last reset: hits[layer_count] and
+ * requests[layer_count] (Q4BoundedExpertCache.layerHits / layerRequests,
+ * Storage/Q4BoundedExpertCache.swift:49-50, 205, 216, printed by the bench at
+ * Sources/QwenFieldfareBench/main.swift:799-805).  A layer outside
+ * [0, layer_count) counts in the nearest partition, the one it is served from. */
+qf_status qf_cache_layer_metrics(const qf_cache *c, int64_t *hits, int64_t *requests);
 /* first[layer_count], count[layer_count]: each partition's slot range. */
 qf_status qf_cache_layer_slots(const qf_cache *c, int32_t *first, int32_t *count);
 
@@ -297,6 +303,19 @@ qf_status qf_tier_fetch(qf_tier *t, const int64_t *host_index, const uint32_t *s
                         void *consumer_stream);
 qf_status qf_tier_stats(const qf_tier *t, int64_t *copies, int64_t *bytes);
 qf_status qf_tier_synchronize(qf_tier *t);
+/* Host-side fault injection (failure-detection tests; the reference's fetch
+ * falls back to a second source when a read fails,
+ * QwenQ4ActiveExpertStreamingRunner.swift:839-866): after `skip` more record
+ * copies, the next `count` are treated as short copies and not issued.  A
+ * failed record copy makes qf_tier_fetch return QF_ERR_IO (the other records
+ * are still copied) and qf_moe_stream_step return QF_ERR_IO without running the
+ * step, with each failed record's slot given back to the expert it held before
+ * (so the cache never maps an expert whose bytes did not arrive; the miss
+ * stays counted, as the reference's telemetry counts it).  skip = count = 0
+ * disarms it. */
+qf_status qf_tier_inject_fault(qf_tier *t, int32_t skip, int32_t count);
+/* Record copies that failed since the tier was created. */
+qf_status qf_tier_failed_copies(const qf_tier *t, int64_t *failed);
 
 /* ---- packed expert store, format v2 (host) ----------------------------- */
 /* Reader of the reference's packed expert files, the source of the host
@@ -462,6 +481,12 @@ qf_status qf_ep_connect(qf_ep *ep, const void *handles);
 void qf_ep_destroy(qf_ep *ep);
 qf_status qf_ep_info(const qf_ep *ep, int32_t *experts_per_rank, int64_t *receive_rows,
                      uint64_t *region_bytes);
+/* Deadline of each bounded wait of the EP kernels (a rank that never arrives),
+ * 1 ms .. 60 s; default 2 s.  After a wait expired (QF_ERR_TIMEOUT from
+ * qf_moe_check) the call's remaining kernels do no work and its output is
+ * undefined; the EP group's counters no longer agree, so every rank destroys
+ * its qf_ep and creates a new one.  The handle itself stays usable. */
+qf_status qf_ep_set_timeout_ms(qf_ep *ep, uint32_t ms);
 /* One MoE block over this rank's T tokens (T <= max_tokens), on the handle's
  * stream.  layer->expert_bank holds this rank's 256/world experts in order
  * (record i = expert rank * 256/world + i); router, coefficient and shared

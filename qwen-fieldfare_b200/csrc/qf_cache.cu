@@ -75,12 +75,17 @@ struct qf_cache {
   std::unordered_map<uint64_t, int> prefetched;  // key -> 1
   uint64_t tick = 0;
   qf_cache_metrics_t m{};
+  // demand hits / lookups per layer partition (Q4BoundedExpertCache.layerHits /
+  // layerRequests, Q4BoundedExpertCache.swift:49-50, 205, 216); reset with m
+  std::vector<int64_t> layer_hits, layer_requests;
   std::string err;
 
   void build_ranges(int requested_layers) {
     const int want = std::max(1, requested_layers);
     layer_count = capacity >= want * kTopKSlots ? want : 1;
     range_first.assign(layer_count, 0);
+    layer_hits.assign(layer_count, 0);
+    layer_requests.assign(layer_count, 0);
     range_count.assign(layer_count, 0);
     if (layer_count == 40) {
       const int remaining = capacity - layer_count * kTopKSlots;
@@ -138,8 +143,34 @@ struct qf_cache {
     return victim;
   }
 
+  // The occupant a miss displaced, kept so that a failed copy can give the slot
+  // back: the slot's bytes are still that occupant's.
+  struct Undo {
+    int slot;
+    uint64_t old_key, old_tick;
+    uint8_t old_seg;
+  };
+
+  // A record copy into `u.slot` failed: the fetched expert is not resident; the
+  // slot holds (and is mapped to) its previous occupant again, as before the
+  // acquire; the miss stays counted (the lookup did miss), the eviction and the
+  // fetched bytes are taken back.
+  void undo_fetch(const Undo& u) {
+    const int s = u.slot;
+    if (slot_seg[s] != kEmpty) key_slot.erase(slot_key[s]);
+    m.fetched_bytes -= static_cast<int64_t>(kRecord);
+    slot_key[s] = u.old_key;
+    slot_seg[s] = u.old_seg;
+    slot_tick[s] = u.old_tick;
+    if (u.old_seg != kEmpty) {
+      key_slot[u.old_key] = s;
+      m.evictions -= 1;
+    }
+  }
+
   int acquire(int32_t layer, const uint32_t* experts, int n, uint32_t* slots, uint32_t* miss_pos,
-              int* n_miss, uint32_t* fetch_expert, uint32_t* fetch_slot, int* n_fetch) {
+              int* n_miss, uint32_t* fetch_expert, uint32_t* fetch_slot, int* n_fetch,
+              Undo* undo = nullptr) {
     const int np = std::min(n, kTopKSlots);
     const int L = layer_of(layer);
     const int a = range_first[L], b = a + range_count[L];
@@ -158,9 +189,11 @@ struct qf_cache {
         prefetched.erase(pf);
       }
       auto it = key_slot.find(key);
+      layer_requests[L] += 1;
       if (it != key_slot.end()) {
         const int s = it->second;
         m.hits += 1;
+        layer_hits[L] += 1;
         slot_tick[s] = tick;
         lock_gen[s] = gen;
         slots[p] = static_cast<uint32_t>(s);
@@ -197,6 +230,7 @@ struct qf_cache {
             break;
           }
       if (victim < 0) victim = 0;
+      if (undo) undo[nf] = Undo{victim, slot_key[victim], slot_tick[victim], slot_seg[victim]};
       if (slot_seg[victim] != kEmpty) {
         const uint64_t old = slot_key[victim];
         auto op = prefetched.find(old);
@@ -291,6 +325,11 @@ struct qf_tier {
   cudaEvent_t done = nullptr;
   int64_t copies = 0;
   int64_t bytes = 0;
+  // host-side fault injection: after `inject_skip` more record copies, the next
+  // `inject_count` are treated as short copies (not issued); failed_copies
+  // counts every record copy that failed
+  int64_t inject_skip = 0, inject_count = 0;
+  int64_t failed_copies = 0;
   // streaming steps: the last step whose kernel reads each slot, an event
   // recorded after each step's kernel, and per-step routing staging
   std::vector<int64_t> slot_last_step;
@@ -388,6 +427,17 @@ qf_status qf_cache_clear(qf_cache* c) {
 qf_status qf_cache_reset_metrics(qf_cache* c) {
   if (!c) return QF_ERR_ARG;
   c->m = qf_cache_metrics_t{};
+  std::fill(c->layer_hits.begin(), c->layer_hits.end(), 0);
+  std::fill(c->layer_requests.begin(), c->layer_requests.end(), 0);
+  return QF_OK;
+}
+
+qf_status qf_cache_layer_metrics(const qf_cache* c, int64_t* hits, int64_t* requests) {
+  if (!c || !hits || !requests) return QF_ERR_ARG;
+  for (int l = 0; l < c->layer_count; l++) {
+    hits[l] = c->layer_hits[l];
+    requests[l] = c->layer_requests[l];
+  }
   return QF_OK;
 }
 
@@ -494,24 +544,64 @@ qf_status qf_tier_arena(const qf_tier* t, void** bank, uint64_t* stride) {
   return QF_OK;
 }
 
+namespace {
+// Issues the record copies on the tier's stream and makes the consumer wait
+// for them.  ok[i] (optional) tells which records were copied; a record whose
+// copy fails (an injected short copy, or a failed enqueue) is skipped and the
+// result is QF_ERR_IO once the others are issued.
+qf_status tier_fetch(qf_tier* t, const int64_t* host_index, const uint32_t* slot, int32_t n,
+                     void* consumer_stream, uint8_t* ok) {
+  TierDevice g(t->device);
+  int failed = 0;
+  for (int i = 0; i < n; i++) {
+    bool good = true;
+    if (t->inject_skip > 0) {
+      t->inject_skip -= 1;
+    } else if (t->inject_count > 0) {
+      t->inject_count -= 1;
+      good = false;  // simulated short copy: nothing issued
+    }
+    if (good && cudaMemcpyAsync(t->arena + static_cast<size_t>(slot[i]) * kRecord,
+                                t->host + static_cast<size_t>(host_index[i]) * t->host_stride, kRecord,
+                                cudaMemcpyHostToDevice, t->side) != cudaSuccess) {
+      cudaGetLastError();
+      good = false;
+    }
+    if (ok) ok[i] = good ? 1 : 0;
+    if (good) {
+      t->copies += 1;
+      t->bytes += static_cast<int64_t>(kRecord);
+    } else {
+      failed += 1;
+    }
+  }
+  t->failed_copies += failed;
+  if (cudaEventRecord(t->done, t->side) != cudaSuccess) return QF_ERR_CUDA;
+  if (cudaStreamWaitEvent(static_cast<cudaStream_t>(consumer_stream), t->done, 0) != cudaSuccess)
+    return QF_ERR_CUDA;
+  return failed ? QF_ERR_IO : QF_OK;
+}
+}  // namespace
+
 qf_status qf_tier_fetch(qf_tier* t, const int64_t* host_index, const uint32_t* slot, int32_t n,
                         void* consumer_stream) {
   if (!t || n < 0 || (n > 0 && (!host_index || !slot))) return QF_ERR_ARG;
   for (int i = 0; i < n; i++)
     if (host_index[i] < 0 || host_index[i] >= t->host_records || slot[i] >= static_cast<uint32_t>(t->slots))
       return QF_ERR_ARG;
-  TierDevice g(t->device);
-  for (int i = 0; i < n; i++) {
-    if (cudaMemcpyAsync(t->arena + static_cast<size_t>(slot[i]) * kRecord,
-                        t->host + static_cast<size_t>(host_index[i]) * t->host_stride, kRecord,
-                        cudaMemcpyHostToDevice, t->side) != cudaSuccess)
-      return QF_ERR_CUDA;
-  }
-  t->copies += n;
-  t->bytes += static_cast<int64_t>(n) * static_cast<int64_t>(kRecord);
-  if (cudaEventRecord(t->done, t->side) != cudaSuccess) return QF_ERR_CUDA;
-  if (cudaStreamWaitEvent(static_cast<cudaStream_t>(consumer_stream), t->done, 0) != cudaSuccess)
-    return QF_ERR_CUDA;
+  return tier_fetch(t, host_index, slot, n, consumer_stream, nullptr);
+}
+
+qf_status qf_tier_inject_fault(qf_tier* t, int32_t skip, int32_t count) {
+  if (!t || skip < 0 || count < 0) return QF_ERR_ARG;
+  t->inject_skip = skip;
+  t->inject_count = count;
+  return QF_OK;
+}
+
+qf_status qf_tier_failed_copies(const qf_tier* t, int64_t* failed) {
+  if (!t || !failed) return QF_ERR_ARG;
+  *failed = t->failed_copies;
   return QF_OK;
 }
 
@@ -591,16 +681,19 @@ qf_status qf_moe_stream_step(qf_moe* h, qf_cache* c, qf_tier* t, const qf_moe_la
   // plan every layer's slots (acquireSlotsParallel per layer), collect copies
   std::vector<int64_t> src;
   std::vector<uint32_t> dst;
+  std::vector<qf_cache::Undo> undo;
   int64_t wait_step = -1;
   for (int l = 0; l < n_layers; l++) {
     uint32_t ex[8], slots[8], fe[8], fs[8];
+    qf_cache::Undo un[8];
     for (int k = 0; k < P; k++) ex[k] = static_cast<uint32_t>(host_idx[l * P + k]);
     int nm = 0, nf = 0;
-    c->acquire(l, ex, P, slots, nullptr, &nm, fe, fs, &nf);
+    c->acquire(l, ex, P, slots, nullptr, &nm, fe, fs, &nf, un);
     for (int f = 0; f < nf; f++) {
       wait_step = std::max(wait_step, t->slot_last_step[fs[f]]);
       src.push_back(static_cast<int64_t>(l) * qf::kExperts + fe[f]);
       dst.push_back(fs[f]);
+      undo.push_back(un[f]);
     }
     for (int k = 0; k < P; k++) {
       sh[l * P + k] = host_idx[l * P + k];
@@ -615,7 +708,15 @@ qf_status qf_moe_stream_step(qf_moe* h, qf_cache* c, qf_tier* t, const qf_moe_la
     if (wait_step > n - kStepRing && wait_step >= 0 &&
         (e = cudaStreamWaitEvent(t->side, t->step_done[wait_step % kStepRing], 0)) != cudaSuccess)
       return cuda_fail(h, e, "stream step: order copies after readers");
-    qf_status st = qf_tier_fetch(t, src.data(), dst.data(), static_cast<int32_t>(src.size()), main);
+    std::vector<uint8_t> ok(src.size(), 0);
+    qf_status st = tier_fetch(t, src.data(), dst.data(), static_cast<int32_t>(src.size()), main, ok.data());
+    if (st == QF_ERR_IO) {
+      // some records did not arrive: give their slots back to the experts they
+      // held (latest first) and run nothing; the caller may retry the step
+      for (size_t i = src.size(); i-- > 0;)
+        if (!ok[i]) c->undo_fetch(undo[i]);
+      return fail(h, st, "stream step: a host-tier record copy failed (step not run)");
+    }
     if (st != QF_OK) return fail(h, st, "stream step: host-tier copy failed");
   }
   if ((e = cudaMemcpyAsync(sd, sh, NP * 3 * sizeof(int32_t), cudaMemcpyHostToDevice, main)) != cudaSuccess)

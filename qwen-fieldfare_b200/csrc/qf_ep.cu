@@ -60,7 +60,7 @@ struct RegionHeader {
   uint32_t magic;
 };
 constexpr uint32_t kRegionMagic = 0x51464550u;
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitNs = 2000000000ull;  // default deadline of every wait: 2 s
 
 __device__ __forceinline__ uint64_t gtime() {
   uint64_t t;
@@ -75,13 +75,14 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 __device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Bounded wait until *c has reached target (wrap-safe).
-__device__ bool wait_counter(const unsigned* c, unsigned target) {
+// Bounded wait until *c has reached target (wrap-safe); false once wait_ns of
+// globaltimer time have passed.
+__device__ bool wait_counter(const unsigned* c, unsigned target, uint64_t wait_ns) {
   const uint64_t t0 = gtime();
   for (unsigned i = 0;; i++) {
     if (static_cast<int>(ld_acquire_sys(c) - target) >= 0) return true;
     if ((i & 15) == 15) {
-      if (gtime() - t0 > kWaitNs) return false;
+      if (gtime() - t0 > wait_ns) return false;
       __nanosleep(100);
     }
   }
@@ -106,6 +107,7 @@ struct EpArgs {
   int* offsets_local;    // [256] first received row of each local expert
   int* q_rows;           // received routed rows (the shared rows follow them)
   int* status;
+  uint64_t wait_ns;      // deadline of each bounded wait
 };
 
 __device__ __forceinline__ unsigned* sig(uint8_t* region, int word) {
@@ -137,10 +139,17 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
   uint8_t* mine = a.peer[a.rank];
 
   // 1. every rank's counts are on this rank's board once all have arrived
-  if (tid == 0) s_ok = wait_counter(sig(mine, kSigArrive), a.epoch * (unsigned)a.world);
+  if (tid == 0) s_ok = wait_counter(sig(mine, kSigArrive), a.epoch * (unsigned)a.world, a.wait_ns);
   __syncthreads();
   if (!s_ok) {
     if (tid == 0) set_status(a.status, kStatusTimeout);
+    // a rank is missing: leave the GEMMs nothing to do (no routed rows, no
+    // shared rows: q_rows < 0 drops the shared tiles from the tile list)
+    if (blockIdx.x == 0) {
+      a.counts_local[tid] = 0;
+      a.offsets_local[tid] = 0;
+      if (tid == 0) *a.q_rows = -1;
+    }
     return;
   }
   const int* board = reinterpret_cast<const int*>(mine + kBoardOff) + par * kMaxRanks * kExperts;
@@ -229,9 +238,13 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
   }
 }
 
-// Waits until every rank's dispatch blocks have delivered (one thread).
-__global__ void k_ep_wait_rows(uint8_t* mine, unsigned target, int* status) {
-  if (threadIdx.x == 0 && !wait_counter(sig(mine, kSigDelivered), target)) set_status(status, kStatusTimeout);
+// Waits until every rank's dispatch blocks have delivered (one thread).  After
+// an expired wait earlier in this call (q_rows < 0) there is nothing to wait for.
+__global__ void k_ep_wait_rows(uint8_t* mine, unsigned target, const int* q_rows, int* status,
+                               uint64_t wait_ns) {
+  if (threadIdx.x == 0 && *(volatile const int*)q_rows >= 0 &&
+      !wait_counter(sig(mine, kSigDelivered), target, wait_ns))
+    set_status(status, kStatusTimeout);
 }
 
 // The owner's result rows are written: tell every rank.
@@ -249,7 +262,9 @@ __global__ void __launch_bounds__(256) k_ep_combine(const __grid_constant__ EpAr
                                                     float* __restrict__ out) {
   __shared__ int s_ok;
   const int t = blockIdx.x;
-  if (threadIdx.x == 0) s_ok = wait_counter(sig(a.peer[a.rank], kSigDone), a.epoch * (unsigned)a.world);
+  if (threadIdx.x == 0)
+    s_ok = *(volatile const int*)a.q_rows >= 0 &&
+           wait_counter(sig(a.peer[a.rank], kSigDone), a.epoch * (unsigned)a.world, a.wait_ns);
   __syncthreads();
   if (!s_ok) {
     if (threadIdx.x == 0) set_status(a.status, kStatusTimeout);
@@ -324,6 +339,7 @@ struct qf_ep {
   int* offsets_local = nullptr;
   int* q_rows = nullptr;
   __half* act = nullptr;
+  uint64_t wait_ns = qf::kWaitNs;
 };
 
 namespace {
@@ -525,11 +541,13 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   a.offsets_local = ep->offsets_local;
   a.q_rows = ep->q_rows;
   a.status = h->d_status;
+  a.wait_ns = ep->wait_ns;
   {
     qf::ProfScope ps(&h->prof, qf::kKDispatch, st);
     qf::k_ep_publish<<<1, qf::kDispThreads, 0, st>>>(a);
     qf::k_ep_dispatch<<<qf::kDispBlocks, qf::kDispThreads, 0, st>>>(a);
-    qf::k_ep_wait_rows<<<1, 32, 0, st>>>(ep->region, a.epoch * (unsigned)ep->world * qf::kDispBlocks, h->d_status);
+    qf::k_ep_wait_rows<<<1, 32, 0, st>>>(ep->region, a.epoch * (unsigned)ep->world * qf::kDispBlocks, ep->q_rows,
+                                         h->d_status, ep->wait_ns);
   }
   e = cudaGetLastError();
   if (e == cudaSuccess) e = qf::tile_list(st, ep->counts_local, ep->offsets_local, T, ep->q_rows, ep->tiles, ep->n_tiles);
@@ -552,6 +570,12 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   e = cudaGetLastError();
   if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: combine");
   ep->epoch++;
+  return QF_OK;
+}
+
+qf_status qf_ep_set_timeout_ms(qf_ep* ep, uint32_t ms) {
+  if (!ep || ms < 1 || ms > 60000) return QF_ERR_ARG;
+  ep->wait_ns = static_cast<uint64_t>(ms) * 1000000ull;
   return QF_OK;
 }
 

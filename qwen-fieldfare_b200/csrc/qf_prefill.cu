@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(256) k_gather_rows(const int* __restrict__ per
 constexpr int kTileRows = 128;
 constexpr int kListThreads = 288;  // one thread per expert and the shared expert
 
-// shared_base (device, optional): first shared row; default T * 8.
+// shared_base (device, optional): first shared row; default T * 8; negative: none.
 __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restrict__ counts,
                                                              const int* __restrict__ offsets, int T,
                                                              const int* __restrict__ shared_base,
@@ -350,8 +350,8 @@ __global__ void __launch_bounds__(kListThreads) k_tile_list(const int* __restric
     cnt = counts[e];
     base = offsets[e];
   } else if (e == kExperts) {
-    cnt = T;
     base = shared_base ? *shared_base : T * kTopK;
+    cnt = base < 0 ? 0 : T;  // a negative shared base (an aborted EP call): no shared rows
   }
   const int full = cnt / kTileRows, rem = cnt % kTileRows;
   s_rem[e] = rem;

@@ -104,6 +104,7 @@ SIGNATURES = {
     "qf_cache_get_metrics": (_S, [_P, C.POINTER(CacheMetrics)]),
     "qf_cache_info": (_S, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
     "qf_cache_layer_slots": (_S, [_P, _P, _P]),
+    "qf_cache_layer_metrics": (_S, [_P, _P, _P]),
     "qf_cache_plan_slots": (_S, [_I, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_uint64),
                                  C.POINTER(C.c_uint64)]),
     "qf_tier_create": (_S, [_I, _I, _P, C.c_int64, C.c_uint64, C.POINTER(_P)]),
@@ -111,6 +112,8 @@ SIGNATURES = {
     "qf_tier_arena": (_S, [_P, C.POINTER(_P), C.POINTER(C.c_uint64)]),
     "qf_tier_fetch": (_S, [_P, _P, _P, _I, _P]),
     "qf_tier_stats": (_S, [_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "qf_tier_inject_fault": (_S, [_P, _I, _I]),
+    "qf_tier_failed_copies": (_S, [_P, C.POINTER(C.c_int64)]),
     "qf_tier_synchronize": (_S, [_P]),
     "qf_moe_stream_step": (_S, [_P, _P, _P, C.POINTER(MoELayerDesc), _I, _P, _P, _P, _P, _P,
                                 C.c_float, _P, C.c_size_t]),
@@ -119,6 +122,7 @@ SIGNATURES = {
     "qf_ep_connect": (_S, [_P, _P]),
     "qf_ep_destroy": (None, [_P]),
     "qf_ep_info": (_S, [_P, C.POINTER(_I), C.POINTER(C.c_int64), C.POINTER(C.c_uint64)]),
+    "qf_ep_set_timeout_ms": (_S, [_P, C.c_uint32]),
     "qf_moe_block_forward_ep": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
                                      C.POINTER(RoutingDesc), _P, _P]),
     "qf_moe_profile_begin": (_S, [_P, _I, _I]),

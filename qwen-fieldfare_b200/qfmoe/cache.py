@@ -109,6 +109,21 @@ class ExpertCache:
         req = m["hits"] + m["misses"]
         return m["hits"] / req if req else 0.0
 
+    def layer_metrics(self):
+        """(hits, requests) per layer since the last reset: the reference cache's
+        layerHits / layerRequests (Q4BoundedExpertCache.swift:49-50)."""
+        hits = np.zeros(self.layer_count, np.int64)
+        req = np.zeros(self.layer_count, np.int64)
+        _ok(lib().qf_cache_layer_metrics(self.h, _np_ptr(hits), _np_ptr(req)),
+            "qf_cache_layer_metrics")
+        return hits, req
+
+    def layer_hit_rates(self):
+        """Per-layer hit rate in percent, 0 for a layer without requests (the
+        bench report's "Layer cache hit rates", main.swift:799-805)."""
+        hits, req = self.layer_metrics()
+        return [float(h) * 100.0 / float(r) if r > 0 else 0.0 for h, r in zip(hits, req)]
+
     def layer_ranges(self):
         first = np.zeros(self.layer_count, np.int32)
         count = np.zeros(self.layer_count, np.int32)
@@ -177,9 +192,15 @@ class HostTier:
         _ok(lib().qf_tier_fetch(self.h, _np_ptr(hi), _np_ptr(sl), hi.size, st), "qf_tier_fetch")
 
     def stats(self):
-        n, b = C.c_int64(), C.c_int64()
+        n, b, f = C.c_int64(), C.c_int64(), C.c_int64()
         _ok(lib().qf_tier_stats(self.h, C.byref(n), C.byref(b)), "qf_tier_stats")
-        return {"copies": n.value, "bytes": b.value}
+        _ok(lib().qf_tier_failed_copies(self.h, C.byref(f)), "qf_tier_failed_copies")
+        return {"copies": n.value, "bytes": b.value, "failed": f.value}
+
+    def inject_fault(self, skip: int, count: int):
+        """After `skip` more record copies, treat the next `count` as short copies
+        (host-side fault injection for failure-detection tests)."""
+        _ok(lib().qf_tier_inject_fault(self.h, skip, count), "qf_tier_inject_fault")
 
     def synchronize(self):
         _ok(lib().qf_tier_synchronize(self.h), "qf_tier_synchronize")

@@ -71,6 +71,10 @@ class ExpertParallel:
             import torch.distributed as dist
             dist.barrier(group=self.group)
 
+    def set_timeout_ms(self, ms: int):
+        """Deadline of each bounded wait on the other ranks (default 2 s)."""
+        check(lib().qf_ep_set_timeout_ms(self.h, ms), self.ctx.h)
+
     def local_layer(self, seed: int, layer: int) -> MoELayerWeights:
         """Seeded synthetic weights with this rank's experts in the bank."""
         return MoELayerWeights.synth(self.ctx, seed, layer, n_records=self.experts_per_rank,

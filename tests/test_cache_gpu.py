@@ -157,3 +157,59 @@ def test_stream_step_argument_errors(ctx, stack):
         tier.fetch([0], [16])
     ctx.check()
     tier.close()
+
+
+def test_stream_step_injected_short_copy(ctx, stack):
+    """Host-side fault injection: one record copy of a step is treated as a
+    short copy.  The step returns QF_ERR_IO without running, the tier counts
+    the failure, the cache does not map the expert whose bytes never arrived,
+    and the same step retried equals the resident chain bitwise."""
+    from qfmoe import HIDDEN, QfError, StackPlan, block_forward, synth_hidden
+    from qfmoe.cache import ExpertCache, HostTier, stream_step
+    layers, host = stack
+    idx, w = trace(4, 31)
+    capacity = N_LAYERS * 10
+    cache = ExpertCache(capacity, layer_count=N_LAYERS)
+    tier = HostTier(0, capacity, host)
+    plan = StackPlan(layers)
+    xs = synth_hidden(SEED, 700, 4).cuda()
+    out = torch.full((1, HIDDEN), float("nan"), device="cuda")
+    ws = ctx.workspace(1)
+    for t in range(2):
+        stream_step(ctx, cache, tier, plan, idx[t], w[t], xs[t:t + 1], None, out, 1e-6, workspace=ws)
+    torch.cuda.synchronize()
+    ctx.check()
+    m0 = cache.metrics_snapshot()
+    s0 = tier.stats()
+    assert s0["failed"] == 0
+    out.fill_(float("nan"))
+    tier.inject_fault(1, 1)  # the second record copy of the next step fails
+    with pytest.raises(QfError, match="QF_ERR_IO"):
+        stream_step(ctx, cache, tier, plan, idx[2], w[2], xs[2:3], None, out, 1e-6, workspace=ws)
+    torch.cuda.synchronize()
+    ctx.check()
+    assert torch.isnan(out).all()  # the step did not run
+    s1 = tier.stats()
+    m1 = cache.metrics_snapshot()
+    assert s1["failed"] == 1
+    misses_2 = m1["misses"] - m0["misses"]
+    assert misses_2 >= 2
+    assert s1["copies"] - s0["copies"] == misses_2 - 1
+    assert m1["fetched_bytes"] - m0["fetched_bytes"] == (misses_2 - 1) * 1_769_472
+    # retry: the failed expert misses again and is fetched; output is exact
+    stream_step(ctx, cache, tier, plan, idx[2], w[2], xs[2:3], None, out, 1e-6, workspace=ws)
+    torch.cuda.synchronize()
+    ctx.check()
+    m2 = cache.metrics_snapshot()
+    assert m2["misses"] - m1["misses"] >= 1
+    assert tier.stats()["failed"] == 1
+    x = xs[2:3]
+    h = None
+    for l in range(N_LAYERS):
+        ti = torch.from_numpy(idx[2, l][None].copy()).cuda()
+        tw = torch.from_numpy(w[2, l][None].copy()).cuda()
+        h = block_forward(ctx, layers[l], x, h, topk_idx=ti, topk_w=tw)
+        if l + 1 < N_LAYERS:
+            x = torch.from_numpy(O.rmsnorm_to_f16(h.cpu().numpy(), 1e-6).view(np.float16)).cuda()
+    assert torch.equal(out, h)
+    tier.close()

@@ -162,3 +162,93 @@ def test_ep_two_gpus_equals_single_gpu_block():
         assert err is None, err
         assert refused, "mismatched max_tokens must be refused"
         assert all(equal), (r, equal)
+
+
+def _timeout_worker(rank, world, port, q, dev):
+    """Rank 1 creates and connects, then leaves the group: it never calls
+    forward, but keeps its exported region alive (rank 0 stores into it) until
+    rank 0 has finished.  Rank 0 calls forward with a 50 ms deadline."""
+    for p in (os.path.join(ROOT, "qwen-fieldfare_b200"), os.path.join(ROOT, "oracle"), ROOT):
+        sys.path.insert(0, p)
+    import datetime
+    import time
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        torch.cuda.set_device(dev)
+        import qfmoe as Q
+        from qfmoe._lib import lib
+        ctx = Q.MoEContext(dev)
+        T = 64
+        ep = Q.ExpertParallel(ctx, rank, world, max_tokens=T)
+        if rank == 1:
+            dist.barrier()  # rank 0 is done with our region
+            lib().qf_ep_destroy(ep.h)
+            ep.h = None
+            q.put((rank, None, None))
+            return
+        ep.set_timeout_ms(50)
+        local = ep.local_layer(SEED, LAYER)
+        x = Q.synth_hidden(SEED, 0, T).cuda()
+        t0 = time.time()
+        ep.forward(local, x)
+        torch.cuda.synchronize()
+        elapsed = time.time() - t0
+        try:
+            ctx.check()
+            status = "ok"
+        except Q.QfError as e:
+            status = str(e)
+        ctx.check()  # the status word was cleared
+        lib().qf_ep_destroy(ep.h)  # the group is broken: no collective close
+        ep.h = None
+        # the handle stays usable: a world-1 EP call and a plain block
+        full = Q.MoELayerWeights.synth(ctx, SEED, LAYER)
+        ep1 = Q.ExpertParallel(ctx, 0, 1, max_tokens=T)
+        out1 = ep1.forward(full, x)
+        ref = Q.block_forward(ctx, full, x)
+        ctx.check()
+        ep1.close()
+        dist.barrier()  # let rank 1 free its region
+        q.put((rank, (status, elapsed, bool(torch.equal(out1, ref))), None))
+    except Exception as exc:  # reported to the parent
+        try:
+            dist.barrier()
+        except Exception:
+            pass
+        q.put((rank, None, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_missing_rank_times_out_and_the_handle_recovers():
+    """A rank that never arrives: rank 0's bounded waits expire after the 50 ms
+    deadline, qf_moe_check reports QF_ERR_TIMEOUT, the call's GEMMs do no work,
+    and a following world-1 call on the same handle equals the single-GPU block.
+    Only rank 0 launches kernels; with two or more GPUs the ranks sit on
+    different GPUs, with one both processes share it (rank 1 only holds its
+    exported region)."""
+    world = 2
+    two = torch.cuda.device_count() >= 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_timeout_worker, args=(r, world, port, q, r if two else 0))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, res, err = q.get(timeout=600)
+        got[r] = (res, err)
+    for p in procs:
+        p.join(timeout=120)
+    assert got[1][1] is None, got[1][1]
+    res, err = got[0]
+    assert err is None, err
+    status, elapsed, equal = res
+    assert "QF_ERR_TIMEOUT" in status, status
+    assert elapsed < 5.0, elapsed  # 50 ms deadlines, not the 2 s default
+    assert equal

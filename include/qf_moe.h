@@ -152,6 +152,50 @@ qf_status qf_moe_dispatch_plan(qf_moe *h, const int32_t *idx, int32_t T, int32_t
                                int32_t *offsets, int32_t *perm, void *workspace,
                                size_t workspace_bytes);
 
+/* ---- pieces of the streaming runner's MoE step -------------------------
+ * The reference runs a token's MoE step in two command buffers so that the
+ * experts already in the cache compute while the missing ones are read
+ * (QwenQ4ActiveExpertStreamingRunner.swift:1227-1381): right after planning,
+ * the shared expert and the HIT subset (:1246-1314); after the reads, the
+ * MISS subset (:1339-1366) and the combine (:1368-1381).  These four entries
+ * replace those dispatches one for one; device pointers, the handle's stream.
+ *
+ * Routed experts of a subset of ONE token's top-8 positions
+ * (qwen_cached_moe_gate_up_subset_q4_simd_f32 + qwen_cached_moe_down_subset_q4_simd_f32,
+ * deltanet.metal:2155-2211):
+ *   layer->expert_bank   the slot arena (record = slot);
+ *   slot_of_pos [8]      the slot of each top-8 position (activeSlotIndicesBuf);
+ *   w [8]                the routing weights of the 8 positions (scoresBuf);
+ *   positions [n]        the subset's positions, distinct, in [0, 8);  n in [0, 8];
+ *   routed_out [2048]    sum over i < 8 of (i < n ? w[p_i] * D_{p_i}(SiLU(G x) * (U x)) : 0),
+ *                        left to right, activations in fp32 (the reference's order).
+ * workspace: qf_moe_workspace_size at T = 1 (256-byte aligned); a call uses it
+ * until its kernels end, so two overlapping calls need two workspaces. */
+qf_status qf_moe_routed_subset(qf_moe *h, const qf_moe_layer *layer, const uint16_t *x,
+                               const int32_t *slot_of_pos, const float *w, const int32_t *positions,
+                               int32_t n, float *routed_out, void *workspace, size_t workspace_bytes);
+/* Shared expert of T <= 64 tokens with its gate:
+ * out[t] = sigmoid(coef[t]) * D_sh(SiLU(G_sh x_t) * (U_sh x_t)), coef = the
+ * shared-gate logits of qf_router_logits_q8 (qwen_shared_gate_up_silu_q4_simd_f32
+ * + qwen_shared_down_gate_q4_simd_f32, deltanet.metal:2050-2122).  workspace:
+ * qf_moe_workspace_size at T. */
+qf_status qf_shared_expert(qf_moe *h, const qf_moe_layer *layer, int32_t T, const uint16_t *x,
+                           const float *coef, float *out, void *workspace, size_t workspace_bytes);
+/* out = ((residual + shared_out) + hit_out) + miss_out over T x 2048 fp32
+ * values; residual, hit_out and miss_out may be NULL (a zero term, as a zero
+ * hit or miss count in qwen_combine_cached_moe_subsets_f32, deltanet.metal:2213-2227). */
+qf_status qf_moe_combine(qf_moe *h, int32_t T, const float *residual, const float *shared_out,
+                         const float *hit_out, const float *miss_out, float *out);
+/* The routed experts of T <= 32768 tokens as one grouped tcgen05 GEMM pair
+ * (absent in the reference, which is decode-only): dispatch plan, row gather,
+ * grouped gate/up and down over a resident bank of 256 experts;
+ * y [T * 8][2048] fp32 (16-B aligned) = D_e(SiLU(G_e x_t) * (U_e x_t)) for
+ * position t * 8 + k, e = idx[t * 8 + k] (unweighted; no shared expert, no
+ * combine).  workspace: qf_moe_grouped_ffn_workspace_size. */
+qf_status qf_moe_grouped_ffn_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
+qf_status qf_moe_grouped_ffn(qf_moe *h, const qf_moe_layer *layer, int32_t T, const uint16_t *x,
+                             const int32_t *idx, float *y, void *workspace, size_t workspace_bytes);
+
 /* Workspace bytes needed by qf_moe_block_forward / qf_moe_stack_forward at T tokens. */
 qf_status qf_moe_workspace_size(qf_moe *h, int32_t T, size_t *bytes);
 

@@ -270,6 +270,80 @@ qf_status qf_router_topk(qf_moe* h, const float* logits, const float* bias, int3
   return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_router_topk");
 }
 
+qf_status qf_moe_routed_subset(qf_moe* h, const qf_moe_layer* layer, const uint16_t* x,
+                               const int32_t* slot_of_pos, const float* w, const int32_t* positions,
+                               int32_t n, float* routed_out, void* workspace, size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  qf::LayerW L;
+  qf_status s = layer_to_w(h, layer, &L);
+  if (s != QF_OK) return s;
+  if (n < 0 || n > qf::kTopK) return fail(h, QF_ERR_ARG, "subset size n must be in [0, 8]");
+  if (!x || !aligned(x, 16) || !routed_out || (n > 0 && (!slot_of_pos || !w || !positions)))
+    return fail(h, QF_ERR_ARG, "x (16-B aligned), slot_of_pos, w, positions and routed_out are required");
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::decode_workspace_bytes(1))
+    return fail(h, QF_ERR_ARG, "workspace too small (qf_moe_workspace_size at T = 1) or not 256-byte aligned");
+  DeviceGuard g(h->device);
+  qf::DecodeWs ws;
+  qf::decode_carve(workspace, 1, &ws);
+  cudaError_t e = qf::routed_subset(stream_of(h), L, h->dims.scale_dtype == QF_SCALE_BF16, x, slot_of_pos, w,
+                                    positions, n, routed_out, ws, h->d_status);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_routed_subset");
+}
+
+qf_status qf_shared_expert(qf_moe* h, const qf_moe_layer* layer, int32_t T, const uint16_t* x,
+                           const float* coef, float* out, void* workspace, size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  qf::LayerW L;
+  qf_status s = layer_to_w(h, layer, &L);
+  if (s != QF_OK) return s;
+  if (T < 1 || T > qf::kDecodeMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 64]");
+  if (!x || !aligned(x, 16) || !coef || !out)
+    return fail(h, QF_ERR_ARG, "x (16-B aligned), coef and out are required");
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::decode_workspace_bytes(T))
+    return fail(h, QF_ERR_ARG, "workspace too small (qf_moe_workspace_size at T) or not 256-byte aligned");
+  DeviceGuard g(h->device);
+  qf::DecodeWs ws;
+  qf::decode_carve(workspace, T, &ws);
+  cudaError_t e = qf::shared_expert(stream_of(h), L, h->dims.scale_dtype == QF_SCALE_BF16, T, x, coef, out, ws);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_shared_expert");
+}
+
+qf_status qf_moe_combine(qf_moe* h, int32_t T, const float* residual, const float* shared_out,
+                         const float* hit_out, const float* miss_out, float* out) {
+  if (!h) return QF_ERR_ARG;
+  if (T < 1 || T > 65536) return fail(h, QF_ERR_ARG, "T must be in [1, 65536]");
+  if (!shared_out || !out) return fail(h, QF_ERR_ARG, "shared_out and out are required");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::combine_subsets(stream_of(h), T, residual, shared_out, hit_out, miss_out, out);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_combine");
+}
+
+qf_status qf_moe_grouped_ffn(qf_moe* h, const qf_moe_layer* layer, int32_t T, const uint16_t* x,
+                             const int32_t* idx, float* y, void* workspace, size_t workspace_bytes) {
+  if (!h) return QF_ERR_ARG;
+  qf::LayerW L;
+  qf_status s = layer_to_w(h, layer, &L);
+  if (s != QF_OK) return s;
+  if (T < 1 || T > qf::kPrefillMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
+  if (L.bank_records < static_cast<uint32_t>(qf::kExperts))
+    return fail(h, QF_ERR_ARG, "the grouped FFN needs a resident bank of 256 experts");
+  if (!x || !aligned(x, 16) || !idx || !y || !aligned(y, 16))
+    return fail(h, QF_ERR_ARG, "x and y (16-B aligned) and idx are required");
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < qf::prefill_workspace_bytes(T))
+    return fail(h, QF_ERR_ARG, "workspace too small (qf_moe_grouped_ffn_workspace_size) or not 256-byte aligned");
+  DeviceGuard g(h->device);
+  cudaError_t e = qf::grouped_ffn_routed(stream_of(h), L, h->dims.scale_dtype == QF_SCALE_BF16, T, x, idx, y,
+                                         workspace, h->d_status, &h->prof);
+  return e == cudaSuccess ? QF_OK : cuda_fail(h, e, "qf_moe_grouped_ffn");
+}
+
+qf_status qf_moe_grouped_ffn_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
+  if (!h || !bytes) return QF_ERR_ARG;
+  if (T < 1 || T > qf::kPrefillMaxTokens) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");
+  *bytes = qf::prefill_workspace_bytes(T);
+  return QF_OK;
+}
+
 qf_status qf_moe_dispatch_workspace_size(qf_moe* h, int32_t T, size_t* bytes) {
   if (!h || !bytes) return QF_ERR_ARG;
   if (T < 1 || T > 32768) return fail(h, QF_ERR_ARG, "T must be in [1, 32768]");

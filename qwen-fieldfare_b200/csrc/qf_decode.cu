@@ -405,13 +405,13 @@ __device__ __forceinline__ void gu_tokens(const uint4 (&wv)[RM][2], const float 
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads) k_gate_up(LayerW L, int T,
                                                       const uint16_t* __restrict__ x,
-                                                      DecodeWs ws) {
+                                                      DecodeWs ws, int with_shared) {
   extern __shared__ __align__(16) float smem[];
   float4* xs4 = reinterpret_cast<float4*>(smem);  // [8 tok][512 chunks] swizzled
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int RM = 2 * kGuRowsPerWarp;  // row-matrices per warp: g0, g1, u0, u1
   const int ng = ws.meta[0];
-  const int n_items = (ng + 1) * kGuRowBlocks;
+  const int n_items = (ng + with_shared) * kGuRowBlocks;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const GroupRef G = group_ref(L, ws, item / kGuRowBlocks, ng, T);
     const int rb = item % kGuRowBlocks;
@@ -525,12 +525,12 @@ __device__ __forceinline__ void dn_tokens(const uint2 (&dw)[kDnRowsPerWarp],
 }
 
 template <bool BF16>
-__global__ void __launch_bounds__(kThreads) k_down(LayerW L, int T, DecodeWs ws) {
+__global__ void __launch_bounds__(kThreads) k_down(LayerW L, int T, DecodeWs ws, int with_shared) {
   extern __shared__ __align__(16) float smem[];
   float4* as4 = reinterpret_cast<float4*>(smem);  // [8 pos][128 chunks] swizzled
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = ws.meta[0];
-  const int n_items = (ng + 1) * kDnRowBlocks;
+  const int n_items = (ng + with_shared) * kDnRowBlocks;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const GroupRef G = group_ref(L, ws, item / kDnRowBlocks, ng, T);
     const int rb = item % kDnRowBlocks;
@@ -674,21 +674,139 @@ cudaError_t decode_block(cudaStream_t st, const LayerW& L, bool bf16, int T, con
   {
     ProfScope ps(prof, kKGateUp, st);
     if (bf16)
-      k_gate_up<true><<<gu_grid, kThreads, kGuSmem, st>>>(L, T, x, ws);
+      k_gate_up<true><<<gu_grid, kThreads, kGuSmem, st>>>(L, T, x, ws, 1);
     else
-      k_gate_up<false><<<gu_grid, kThreads, kGuSmem, st>>>(L, T, x, ws);
+      k_gate_up<false><<<gu_grid, kThreads, kGuSmem, st>>>(L, T, x, ws, 1);
   }
   {
     ProfScope ps(prof, kKDown, st);
     if (bf16)
-      k_down<true><<<dn_grid, kThreads, kDnSmem, st>>>(L, T, ws);
+      k_down<true><<<dn_grid, kThreads, kDnSmem, st>>>(L, T, ws, 1);
     else
-      k_down<false><<<dn_grid, kThreads, kDnSmem, st>>>(L, T, ws);
+      k_down<false><<<dn_grid, kThreads, kDnSmem, st>>>(L, T, ws, 1);
   }
   {
     ProfScope ps(prof, kKCombine, st);
     k_combine<<<T, kThreads, 0, st>>>(T, residual, ws, out, x16_next, eps);
   }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- subsets
+// The streaming runner's split of one token's routed experts into the
+// positions whose records are resident (hits) and those still being fetched
+// (misses): qwen_cached_moe_gate_up_subset_q4_simd_f32 and
+// qwen_cached_moe_down_subset_q4_simd_f32 (deltanet.metal:2155-2211), the
+// shared expert with its gate (:2050-2122) and the subset combine (:2213-2227).
+// The gate/up and down arithmetic is k_gate_up / k_down's (one group per
+// position: the 8 positions of a token name 8 distinct records).
+
+// Plan of a subset of token 0's top-8: group i = positions[i] alone, record
+// slot_of_pos[positions[i]].  A position outside [0, 8) or a record outside
+// the bank is reported (QF_ERR_DEVICE) and served by record 0.
+__global__ void k_subset_plan(const int* __restrict__ slot_of_pos, const int* __restrict__ positions, int n,
+                              uint32_t bank_records, DecodeWs ws, int* status) {
+  const int i = threadIdx.x;
+  if (i == 0) ws.meta[0] = n;
+  if (i >= n) return;
+  int pos = positions[i];
+  if (pos < 0 || pos >= kTopK) {
+    set_status(status, kStatusDevice);
+    pos = 0;
+  }
+  int rec = slot_of_pos[pos];
+  if (rec < 0 || static_cast<uint32_t>(rec) >= bank_records) {
+    set_status(status, kStatusDevice);
+    rec = 0;
+  }
+  ws.group_rec[i] = rec;
+  ws.group_start[i] = i;
+  ws.group_cnt[i] = 1;
+  ws.sorted_pos[i] = pos;
+}
+
+// routed_out[r] = sum over i < 8 of (i < n ? y[positions[i]][r] * w[positions[i]] : 0),
+// left to right (the reference's eight simdgroup partials, :2197-2210).
+__global__ void __launch_bounds__(kThreads) k_subset_sum(const int* __restrict__ positions, int n,
+                                                         const float* __restrict__ w, DecodeWs ws,
+                                                         float* __restrict__ routed_out) {
+  const int r = blockIdx.x * kThreads + threadIdx.x;
+  if (r >= kHidden) return;
+  float part[kTopK];
+#pragma unroll
+  for (int i = 0; i < kTopK; i++) {
+    part[i] = 0.f;
+    if (i < n) {
+      const int pos = min(max(positions[i], 0), kTopK - 1);
+      part[i] = __fmul_rn(ws.y_part[static_cast<size_t>(pos) * kHidden + r], w[pos]);
+    }
+  }
+  float acc = part[0];
+#pragma unroll
+  for (int i = 1; i < kTopK; i++) acc = __fadd_rn(acc, part[i]);
+  routed_out[r] = acc;
+}
+
+// shared_out[t][r] = y_sh[t][r] * (1 / (1 + exp(-coef[t])))   (:2117-2120)
+__global__ void __launch_bounds__(kThreads) k_shared_gate(int T, const float* __restrict__ coef, DecodeWs ws,
+                                                          float* __restrict__ out) {
+  const int t = blockIdx.y, r = blockIdx.x * kThreads + threadIdx.x;
+  if (r >= kHidden) return;
+  const float coeff = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-coef[t])));
+  out[static_cast<size_t>(t) * kHidden + r] = __fmul_rn(ws.y_sh[static_cast<size_t>(t) * kHidden + r], coeff);
+}
+
+// out = ((residual + shared) + hit) + miss; a NULL term is 0 (:2213-2227)
+__global__ void __launch_bounds__(kThreads) k_combine_subsets(int n, const float* __restrict__ residual,
+                                                              const float* __restrict__ shared_out,
+                                                              const float* __restrict__ hit,
+                                                              const float* __restrict__ miss,
+                                                              float* __restrict__ out) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= n) return;
+  const float res = residual ? residual[i] : 0.f;
+  const float h = hit ? hit[i] : 0.f;
+  const float m = miss ? miss[i] : 0.f;
+  out[i] = __fadd_rn(__fadd_rn(__fadd_rn(res, shared_out[i]), h), m);
+}
+
+cudaError_t routed_subset(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* x,
+                          const int* slot_of_pos, const float* w, const int* positions, int n,
+                          float* routed_out, const DecodeWs& ws, int* status) {
+  k_subset_plan<<<1, 32, 0, st>>>(slot_of_pos, positions, n, L.bank_records, ws, status);
+  if (n > 0) {
+    if (bf16) {
+      k_gate_up<true><<<n * kGuRowBlocks, kThreads, kGuSmem, st>>>(L, 1, x, ws, 0);
+      k_down<true><<<n * kDnRowBlocks, kThreads, kDnSmem, st>>>(L, 1, ws, 0);
+    } else {
+      k_gate_up<false><<<n * kGuRowBlocks, kThreads, kGuSmem, st>>>(L, 1, x, ws, 0);
+      k_down<false><<<n * kDnRowBlocks, kThreads, kDnSmem, st>>>(L, 1, ws, 0);
+    }
+  }
+  k_subset_sum<<<kHidden / kThreads, kThreads, 0, st>>>(positions, n, w, ws, routed_out);
+  return cudaGetLastError();
+}
+
+cudaError_t shared_expert(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                          const float* coef, float* out, const DecodeWs& ws) {
+  // no routed groups: k_gate_up / k_down run only the shared expert's items
+  cudaError_t e = cudaMemsetAsync(ws.meta, 0, sizeof(int), st);
+  if (e != cudaSuccess) return e;
+  if (bf16) {
+    k_gate_up<true><<<kGuRowBlocks, kThreads, kGuSmem, st>>>(L, T, x, ws, 1);
+    k_down<true><<<kDnRowBlocks, kThreads, kDnSmem, st>>>(L, T, ws, 1);
+  } else {
+    k_gate_up<false><<<kGuRowBlocks, kThreads, kGuSmem, st>>>(L, T, x, ws, 1);
+    k_down<false><<<kDnRowBlocks, kThreads, kDnSmem, st>>>(L, T, ws, 1);
+  }
+  k_shared_gate<<<dim3(kHidden / kThreads, T), kThreads, 0, st>>>(T, coef, ws, out);
+  return cudaGetLastError();
+}
+
+cudaError_t combine_subsets(cudaStream_t st, int T, const float* residual, const float* shared_out,
+                            const float* hit, const float* miss, float* out) {
+  const int n = T * kHidden;
+  k_combine_subsets<<<(n + kThreads - 1) / kThreads, kThreads, 0, st>>>(n, residual, shared_out, hit, miss, out);
   return cudaGetLastError();
 }
 

@@ -36,6 +36,14 @@ struct DecodeWs {
 };
 
 size_t decode_workspace_bytes(int T);
+// Subset pieces of the streaming runner (T = 1 for routed_subset).
+cudaError_t routed_subset(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* x,
+                          const int* slot_of_pos, const float* w, const int* positions, int n,
+                          float* routed_out, const DecodeWs& ws, int* status);
+cudaError_t shared_expert(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                          const float* coef, float* out, const DecodeWs& ws);
+cudaError_t combine_subsets(cudaStream_t st, int T, const float* residual, const float* shared_out,
+                            const float* hit, const float* miss, float* out);
 void decode_carve(void* base, int T, DecodeWs* ws);
 cudaError_t decode_init_attributes();
 
@@ -125,6 +133,8 @@ cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bo
 // ---- prefill path, T > 64 (qf_prefill.cu)
 constexpr int kPrefillMaxTokens = 32768;
 size_t prefill_workspace_bytes(int T);
+cudaError_t grouped_ffn_routed(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                               const int* idx, float* y, void* workspace, int* status, Prof* prof);
 cudaError_t prefill_init_attributes();
 cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
                                   const uint16_t* x, float* logits, float* coef);

@@ -168,79 +168,74 @@ __device__ __forceinline__ float h16_to_f32(uint16_t u) {
 // accumulates dot = fma-chain of 8 products, acc = fma(s, dot, acc),
 // acc = fma(b, xsum, acc); the lanes are then summed with the xor butterfly
 // 16, 8, 4, 2, 1 (simd_sum), so the logits are bit-identical to the decode
-// router and the oracle.  Each warp carries 2 router rows x 8 tokens at once:
-// every x value a lane reads from shared memory feeds 2 rows, and each row's
-// codes are read as 256 contiguous bytes per block.  In shared memory the two
-// 16-byte halves of 8-element group c are swapped when bit 2 of c is set, so
-// the eight lanes of a quarter-warp (32 bytes apart) read distinct banks.  An extra warp computes
-// the shared-gate coefficient per token as the reference's single sequential
-// chain (qwen_gemv_q8_affine, deltanet.metal:863-902).
+// router and the oracle.  A CTA computes 32 router rows x 8 tokens: each warp
+// holds 4 rows' codes of the current block in registers (converted once) and
+// streams the 8 tokens' x slices from shared memory, where x is staged once
+// per CTA as fp32 (exact widening of the fp16 input), so every 32-byte read
+// of x (8 wavefronts) and of its 8-value sum (1 wavefront) feeds 4 rows x 10
+// FMAs.  In shared memory the two 16-byte halves of 8-element group c are
+// swapped when bit 2 of c is set, so the eight lanes of a quarter-warp (32
+// bytes apart) read distinct banks.  The last row of CTAs (blockIdx.y == 8)
+// computes the shared-gate coefficient instead, one lane per token, as the
+// reference's single sequential chain (qwen_gemv_q8_affine,
+// deltanet.metal:863-902).
 constexpr int kRtTok = 8;
 constexpr int kRtWarps = 8;
-constexpr int kRtRowsPerWarp = 2;
+constexpr int kRtRowsPerWarp = 4;
 constexpr int kRtRows = kRtWarps * kRtRowsPerWarp;  // 32 router rows per CTA
-constexpr int kRtThreads = (kRtWarps + 1) * 32;
+constexpr int kRtThreads = kRtWarps * 32;
+constexpr int kRtRowBlocks = kExperts / kRtRows;  // + 1 row of coefficient CTAs
 constexpr size_t kRtSmem = sizeof(float) * (kRtTok * kHidden + kRtTok * 256);
 
 template <bool BF16>
-__global__ void __launch_bounds__(kRtThreads, 3) k_router_prefill(LayerW L, int T,
+__global__ void __launch_bounds__(kRtThreads, 2) k_router_prefill(LayerW L, int T,
                                                                   const uint16_t* __restrict__ x,
                                                                   float* __restrict__ logits,
                                                                   float* __restrict__ coef) {
   extern __shared__ float4 rsm4[];
-  float* xs = reinterpret_cast<float*>(rsm4);  // [8][2048]
+  float* xs = reinterpret_cast<float*>(rsm4);  // [8][2048], group halves swizzled
   float* xsum = xs + kRtTok * kHidden;         // [8][8 blk][32 lanes]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * kRtTok;
   const int tn = min(kRtTok, T - t0);
+  // x rows (zero past the last token) and the in-order sum of every 8-value group
   for (int i = tid; i < kRtTok * (kHidden / 8); i += kRtThreads) {
     const int t = i / (kHidden / 8), c = i % (kHidden / 8);
-    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
-    if (t < tn) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
-      const __half2* h = reinterpret_cast<const __half2*>(&v);
-      const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), cc = __half22float2(h[2]),
-                   dd = __half22float2(h[3]);
-      lo = make_float4(a.x, a.y, b.x, b.y);
-      hi = make_float4(cc.x, cc.y, dd.x, dd.y);
-    }
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t < tn) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), cc = __half22float2(h[2]),
+                 dd = __half22float2(h[3]);
     float4* d = reinterpret_cast<float4*>(xs + t * kHidden + c * 8);
     const int sw = (c >> 2) & 1;
-    d[sw] = lo;
-    d[sw ^ 1] = hi;
+    d[sw] = make_float4(a.x, a.y, b.x, b.y);
+    d[sw ^ 1] = make_float4(cc.x, cc.y, dd.x, dd.y);
+    float sm = a.x;
+    sm = __fadd_rn(sm, a.y);
+    sm = __fadd_rn(sm, b.x);
+    sm = __fadd_rn(sm, b.y);
+    sm = __fadd_rn(sm, cc.x);
+    sm = __fadd_rn(sm, cc.y);
+    sm = __fadd_rn(sm, dd.x);
+    sm = __fadd_rn(sm, dd.y);
+    xsum[i] = sm;  // i = t * 256 + blk * 32 + lane
   }
   __syncthreads();
-  for (int i = tid; i < kRtTok * 256; i += kRtThreads) {
-    const int c = i & 255;  // 8-element group within the token row
-    const float4* e = reinterpret_cast<const float4*>(xs + (i >> 8) * kHidden + c * 8);
-    const int sw = (c >> 2) & 1;
-    const float4 lo = e[sw], hi = e[sw ^ 1];
-    float v = lo.x;
-    v = __fadd_rn(v, lo.y);
-    v = __fadd_rn(v, lo.z);
-    v = __fadd_rn(v, lo.w);
-    v = __fadd_rn(v, hi.x);
-    v = __fadd_rn(v, hi.y);
-    v = __fadd_rn(v, hi.z);
-    v = __fadd_rn(v, hi.w);
-    xsum[i] = v;
-  }
-  __syncthreads();
-  if (warp < kRtWarps) {
-    const int rbase = blockIdx.y * kRtRows + warp * kRtRowsPerWarp;
+  if (blockIdx.y < kRtRowBlocks) {
+    constexpr int R = kRtRowsPerWarp;
+    const int rbase = blockIdx.y * kRtRows + warp * R;
     const uint8_t* wrow = L.rw + (size_t)rbase * kHidden + lane * 8;
-    const int sw = (lane >> 2) & 1;
-    float acc[kRtRowsPerWarp][kRtTok];
+    float acc[R][kRtTok];
 #pragma unroll
-    for (int r = 0; r < kRtRowsPerWarp; r++)
+    for (int r = 0; r < R; r++)
 #pragma unroll
       for (int t = 0; t < kRtTok; t++) acc[r][t] = 0.f;
-    uint2 wn[kRtRowsPerWarp];
-    uint16_t sn[kRtRowsPerWarp], bn[kRtRowsPerWarp];
+    uint2 wn[R];
+    uint16_t sn[R], bn[R];
     auto fetch = [&](int blk) {
       const int g = blk * 4 + (lane >> 3);
 #pragma unroll
-      for (int r = 0; r < kRtRowsPerWarp; r++) {
+      for (int r = 0; r < R; r++) {
         wn[r] = __ldg(reinterpret_cast<const uint2*>(wrow + (size_t)r * kHidden + blk * 256));
         sn[r] = __ldg(L.rs + (size_t)(rbase + r) * (kHidden / kGroup) + g);
         bn[r] = __ldg(L.rb + (size_t)(rbase + r) * (kHidden / kGroup) + g);
@@ -249,9 +244,9 @@ __global__ void __launch_bounds__(kRtThreads, 3) k_router_prefill(LayerW L, int 
     fetch(0);
 #pragma unroll 1
     for (int blk = 0; blk < 8; blk++) {
-      float q[kRtRowsPerWarp][8], sc[kRtRowsPerWarp], bi[kRtRowsPerWarp];
+      float q[R][8], sc[R], bi[R];
 #pragma unroll
-      for (int r = 0; r < kRtRowsPerWarp; r++) {
+      for (int r = 0; r < R; r++) {
 #pragma unroll
         for (int k = 0; k < 4; k++) {
           q[r][k] = byte_f(wn[r].x, k);
@@ -261,13 +256,14 @@ __global__ void __launch_bounds__(kRtThreads, 3) k_router_prefill(LayerW L, int 
         bi[r] = h16_to_f32<BF16>(bn[r]);
       }
       if (blk + 1 < 8) fetch(blk + 1);
+      const int sw = (lane >> 2) & 1;
 #pragma unroll
       for (int t = 0; t < kRtTok; t++) {
         const float4* e4 = reinterpret_cast<const float4*>(xs + t * kHidden + blk * 256 + lane * 8);
         const float4 a = e4[sw], b = e4[sw ^ 1];
         const float xsm = xsum[t * 256 + blk * 32 + lane];
 #pragma unroll
-        for (int r = 0; r < kRtRowsPerWarp; r++) {
+        for (int r = 0; r < R; r++) {
           float dot = 0.f;
           dot = __fmaf_rn(q[r][0], a.x, dot);
           dot = __fmaf_rn(q[r][1], a.y, dot);
@@ -282,13 +278,13 @@ __global__ void __launch_bounds__(kRtThreads, 3) k_router_prefill(LayerW L, int 
       }
     }
 #pragma unroll
-    for (int r = 0; r < kRtRowsPerWarp; r++)
+    for (int r = 0; r < R; r++)
 #pragma unroll
       for (int t = 0; t < kRtTok; t++) {
         const float v = warp_sum(acc[r][t]);
         if (lane == ((r * kRtTok + t) & 31) && t < tn) logits[(size_t)(t0 + t) * kExperts + rbase + r] = v;
       }
-  } else if (coef && blockIdx.y == 0) {
+  } else if (coef && warp == 0) {
     const int t = lane;
     if (t < tn) {
       const float* xt = xs + t * kHidden;
@@ -538,7 +534,11 @@ constexpr int kSbWin = 8;                        // steps per scale/bias window
 constexpr int kSbBufs = 2;
 constexpr int kSbHalf = 2 * 128 * kSbWin * 2;    // scales (or biases) of one window: 4 KB
 constexpr int kRingBytes = kTokStages * kTokStageBytes + kCodeStages * kCodeStageBytes + kSbBufs * 2 * kSbHalf;
-// TMEM columns: acc0 [0,128) | acc1 [128,256) | A stage s at 256 + 64 s (block 0 +0, block 1 +32)
+// TMEM columns: acc0 [0,128) | acc1 [128,256) | A stage s at 256 + 64 s (block 0 +0, block 1 +32).
+// A unit of <= kSmallAcc token rows accumulates in one half of each block's
+// 128 columns (half = unit index & 1), so consecutive small units are
+// double-buffered: the MMAs of one run while the epilogue drains the other.
+constexpr int kSmallAcc = 64;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = 256;
 
@@ -547,8 +547,8 @@ struct GemmSync {
   uint64_t tok_empty[kTokStages];
   uint64_t a_full[kAStages];
   uint64_t a_empty[kAStages];
-  uint64_t acc_full;
-  uint64_t acc_empty;
+  uint64_t acc_full[2];   // per accumulator half (columns +0 / +64 of each block)
+  uint64_t acc_empty[2];
   uint64_t code_full[kCodeStages];
   uint64_t code_empty[kCodeStages];
   uint64_t sb_full[kSbBufs];
@@ -646,8 +646,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       mbar_init(&sy->a_full[s], 8);
       mbar_init(&sy->a_empty[s], 2);
     }
-    mbar_init(&sy->acc_full, 2);
-    mbar_init(&sy->acc_empty, 8);
+    for (int h = 0; h < 2; h++) {
+      mbar_init(&sy->acc_full[h], 2);
+      mbar_init(&sy->acc_empty[h], 8);
+    }
     for (int s = 0; s < kCodeStages; s++) {
       mbar_init(&sy->code_full[s], 1);
       mbar_init(&sy->code_empty[s], 8);
@@ -713,6 +715,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
     // ---------------- epilogue: TMEM -> SiLU(g)*u fp16 act / weighted fp32 y
     const int eq = warp & 3, half = (warp - 8) >> 2, et = threadIdx.x - 256;
     const uint32_t lrow = (uint32_t)(eq * 32) << 16;
+    uint32_t acc_use[2] = {0u, 0u};
     for (int i = 0; i < my_units; i++) {
       const int u = blockIdx.x + i * G;
       const int4 t = a.tiles[u / PARTS];
@@ -743,8 +746,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
         }
         named_sync(2, kEpiThreads);
       }
-      if (!mbar_wait(&sy->acc_full, i & 1)) ok = false;
+      // accumulator halves: a tile of <= 64 rows uses half i & 1 alone, a
+      // larger one both (acc_use counts each half's earlier units)
+      const bool small_u = n <= kSmallAcc;
+      const bool use0 = !small_u || (i & 1) == 0, use1 = !small_u || (i & 1) == 1;
+      if (use0 && !mbar_wait(&sy->acc_full[0], acc_use[0] & 1)) ok = false;
+      if (use1 && !mbar_wait(&sy->acc_full[1], acc_use[1] & 1)) ok = false;
       tc_fence_after();
+      const uint32_t hcol = small_u ? (uint32_t)(i & 1) * kSmallAcc : 0u;
       const int cbeg = half * (kTileRows / 2), cend = min(n, cbeg + kTileRows / 2);
       if (MODE == 0) {
         const int f = part * 128 + eq * 32 + lane;
@@ -752,8 +761,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
         __half* dst = a.act + (size_t)pb * kInter + fp;
         for (int c0 = cbeg; c0 < cend; c0 += 16) {
           uint32_t g[16], v[16];
-          tmem_ld16(tmem + lrow + c0, g);
-          tmem_ld16(tmem + lrow + 128 + c0, v);
+          tmem_ld16(tmem + lrow + hcol + c0, g);
+          tmem_ld16(tmem + lrow + 128 + hcol + c0, v);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 16; j++)
@@ -765,8 +774,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
         const int f = part * 256 + eq * 32 + lane;
         for (int c0 = cbeg; c0 < cend; c0 += 32) {
           uint32_t v0[32], v1[32];
-          tmem_ld32(tmem + lrow + c0, v0);
-          tmem_ld32(tmem + lrow + 128 + c0, v1);
+          tmem_ld32(tmem + lrow + hcol + c0, v0);
+          tmem_ld32(tmem + lrow + 128 + hcol + c0, v1);
           tmem_ld_wait();
           if (a.ep.ret) {
 #pragma unroll
@@ -792,7 +801,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sy->acc_empty);
+      if (lane == 0) {
+        if (use0) mbar_arrive(&sy->acc_empty[0]);
+        if (use1) mbar_arrive(&sy->acc_empty[1]);
+      }
+      acc_use[0] += use0 ? 1u : 0u;
+      acc_use[1] += use1 ? 1u : 0u;
     }
     // peer stores are visible system-wide before the kernel that signals them runs
     if (MODE == 1 && a.ep.ret) __threadfence_system();
@@ -800,13 +814,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
     // ---------------- MMA issue: warp 16 -> block 0 / acc0, warp 17 -> block 1 / acc1
     if (lane == 0) {
       const uint32_t blk = (uint32_t)(warp - kMmaWarp);
-      const uint32_t dacc = tmem + blk * 128;
       int gs = 0;
+      uint32_t acc_use[2] = {0u, 0u};
       for (int i = 0; i < my_units; i++) {
         const int u = blockIdx.x + i * G;
-        const uint32_t N = (uint32_t)((a.tiles[u / PARTS].z + 15) & ~15);
+        const int rows = a.tiles[u / PARTS].z;
+        const uint32_t N = (uint32_t)((rows + 15) & ~15);
         const uint32_t idesc = (1u << 4) | ((N >> 3) << 17) | ((128u >> 4) << 24);
-        if (!mbar_wait(&sy->acc_empty, (i & 1) ^ 1)) ok = false;
+        // the same half choice as the epilogue: a small tile takes half i & 1
+        const bool small_u = rows <= kSmallAcc;
+        const bool use0 = !small_u || (i & 1) == 0, use1 = !small_u || (i & 1) == 1;
+        const uint32_t dacc = tmem + blk * 128 + (small_u ? (uint32_t)(i & 1) * kSmallAcc : 0u);
+        if (use0 && !mbar_wait(&sy->acc_empty[0], (acc_use[0] & 1) ^ 1)) ok = false;
+        if (use1 && !mbar_wait(&sy->acc_empty[1], (acc_use[1] & 1) ^ 1)) ok = false;
         tc_fence_after();
         for (int ks = 0; ks < KS; ks++, gs++) {
           const int ts = gs % kTokStages, as = gs % kAStages;
@@ -820,7 +840,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
           tc_commit(&sy->tok_empty[ts]);
           tc_commit(&sy->a_empty[as]);
         }
-        tc_commit(&sy->acc_full);
+        if (use0) tc_commit(&sy->acc_full[0]);
+        if (use1) tc_commit(&sy->acc_full[1]);
+        acc_use[0] += use0 ? 1u : 0u;
+        acc_use[1] += use1 ? 1u : 0u;
       }
     }
   } else if (warp == kLoadWarp && lane == 0) {
@@ -1060,7 +1083,7 @@ cudaError_t prefill_init_attributes() {
 
 cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
                                   const uint16_t* x, float* logits, float* coef) {
-  const dim3 grid((T + kRtTok - 1) / kRtTok, kExperts / kRtRows);
+  const dim3 grid((T + kRtTok - 1) / kRtTok, kRtRowBlocks + (coef ? 1 : 0));
   if (bf16)
     k_router_prefill<true><<<grid, kRtThreads, kRtSmem, st>>>(L, T, x, logits, coef);
   else
@@ -1115,6 +1138,42 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
       k_grouped<false, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
   }
   return cudaGetLastError();
+}
+
+// The routed experts of T tokens without the shared expert or the combine:
+// y[t * 8 + k] = D_e(SiLU(G_e x_t) * (U_e x_t)), e = idx[t * 8 + k], through
+// the dispatch plan, the row gather and the grouped GEMMs of the block (the
+// tile list gets a negative shared base, so it holds no shared-expert tiles).
+// Workspace: prefill_workspace_bytes(T).
+cudaError_t grouped_ffn_routed(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,
+                               const int* idx, float* y, void* workspace, int* status, Prof* prof) {
+  const size_t P = static_cast<size_t>(T) * kTopK;
+  const size_t max_tiles = max_tiles_for(T);
+  char* p = static_cast<char*>(workspace);
+  auto take = [&](size_t n) {
+    char* q = p;
+    p += al256(n);
+    return q;
+  };
+  int* counts = reinterpret_cast<int*>(take(4 * (kExperts + 1)));
+  int* offsets = reinterpret_cast<int*>(take(4 * (kExperts + 1)));
+  int* perm = reinterpret_cast<int*>(take(4 * P));
+  int* plan_ws = reinterpret_cast<int*>(take(dispatch_workspace_bytes(T)));
+  int4* tiles = reinterpret_cast<int4*>(take(16 * max_tiles));
+  int* n_tiles = reinterpret_cast<int*>(take(16));
+  int* no_shared = n_tiles + 1;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(take(2 * P * kHidden));
+  __half* act = reinterpret_cast<__half*>(take(2 * P * kInter));
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaMemsetAsync(no_shared, 0xFF, sizeof(int), st);  // -1: no shared rows
+  if (e == cudaSuccess) e = dispatch_plan_ws(st, idx, T, counts, offsets, perm, plan_ws, status);
+  if (e != cudaSuccess) return e;
+  k_tile_list<<<1, kListThreads, 0, st>>>(counts, offsets, T, no_shared, tiles, n_tiles);
+  k_gather_rows<<<(unsigned)((P + 7) / 8), 256, 0, st>>>(perm, (int)P, 0, reinterpret_cast<const uint4*>(x),
+                                                          reinterpret_cast<uint4*>(xs));
+  return grouped_ffn(st, L, bf16, xs, P, act, y, perm, tiles, n_tiles, max_tiles, sms, status, prof, nullptr);
 }
 
 cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, const uint16_t* x,

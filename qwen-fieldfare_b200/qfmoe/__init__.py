@@ -11,4 +11,5 @@ from .moe import (  # noqa: F401
     DECODE_MAX_TOKENS, EXPERTS, HIDDEN, INTER, OFF, RECORD_BYTES, SHARED_EXPERT, TOPK,
     MoEContext, MoELayerWeights, StackPlan, block_forward, block_forward_prenorm, dispatch_plan, lm_head, router_logits,
     profile_begin, profile_end, router_topk, stack_forward, synth_hidden, synth_records,
+    combine, grouped_ffn, routed_subset, shared_expert,
 )

@@ -89,6 +89,11 @@ SIGNATURES = {
     "qf_moe_dispatch_workspace_size": (_S, [_P, _I, C.POINTER(C.c_size_t)]),
     "qf_moe_dispatch_plan": (_S, [_P, _P, _I, _P, _P, _P, _P, C.c_size_t]),
     "qf_moe_workspace_size": (_S, [_P, _I, C.POINTER(C.c_size_t)]),
+    "qf_moe_routed_subset": (_S, [_P, C.POINTER(MoELayerDesc), _P, _P, _P, _P, _I, _P, _P, C.c_size_t]),
+    "qf_shared_expert": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P, _P, C.c_size_t]),
+    "qf_moe_combine": (_S, [_P, _I, _P, _P, _P, _P, _P]),
+    "qf_moe_grouped_ffn_workspace_size": (_S, [_P, _I, C.POINTER(C.c_size_t)]),
+    "qf_moe_grouped_ffn": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P, _P, C.c_size_t]),
     "qf_moe_block_forward": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
                                   C.POINTER(RoutingDesc), _P, _P, _P, C.c_size_t]),
     "qf_moe_stack_forward": (_S, [_P, C.POINTER(MoELayerDesc), _I, _I, _P, _P, _P, C.c_float,

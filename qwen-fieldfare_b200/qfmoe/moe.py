@@ -234,6 +234,75 @@ def block_forward(ctx: MoEContext, layer: MoELayerWeights, x: torch.Tensor,
     return (out, idx, w) if return_routing else out
 
 
+def routed_subset(ctx: MoEContext, layer: MoELayerWeights, x: torch.Tensor, slot_of_pos: torch.Tensor,
+                  w: torch.Tensor, positions, out: torch.Tensor | None = None,
+                  workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed experts of a subset of one token's top-8 positions (the hit or the
+    miss set of the streaming runner): fp32 [1, 2048] = sum over the listed
+    positions, in list order, of w[p] * expert_p(x) (qf_moe_routed_subset).
+    layer.bank is the slot arena; slot_of_pos int32 [8] and w fp32 [8] on the
+    device; positions: a list of distinct ints in [0, 8)."""
+    _check_x(x)
+    if x.shape[0] != 1:
+        raise ValueError("a subset is one token's")
+    pos = torch.tensor(list(positions) + [0] * (TOPK - len(positions)), dtype=torch.int32,
+                       device=ctx.device)
+    if out is None:
+        out = torch.empty((1, HIDDEN), dtype=torch.float32, device=ctx.device)
+    ws = workspace if workspace is not None else ctx.workspace(1)
+    ctx._bind_stream()
+    d = layer.desc()
+    check(lib().qf_moe_routed_subset(ctx.h, C.byref(d), _ptr(x), _ptr(slot_of_pos), _ptr(w), _ptr(pos),
+                                     len(positions), _ptr(out), _ptr(ws), ws.numel()), ctx.h)
+    return out
+
+
+def shared_expert(ctx: MoEContext, layer: MoELayerWeights, x: torch.Tensor, coef: torch.Tensor,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """sigmoid(coef[t]) * shared_expert(x_t) for T <= 64 tokens (qf_shared_expert)."""
+    _check_x(x)
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, HIDDEN), dtype=torch.float32, device=ctx.device)
+    ws = ctx.workspace(T)
+    ctx._bind_stream()
+    d = layer.desc()
+    check(lib().qf_shared_expert(ctx.h, C.byref(d), T, _ptr(x), _ptr(coef), _ptr(out), _ptr(ws),
+                                 ws.numel()), ctx.h)
+    return out
+
+
+def combine(ctx: MoEContext, shared_out: torch.Tensor, residual: torch.Tensor | None = None,
+            hit: torch.Tensor | None = None, miss: torch.Tensor | None = None,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """((residual + shared_out) + hit) + miss, a None term being 0 (qf_moe_combine)."""
+    T = shared_out.shape[0]
+    if out is None:
+        out = torch.empty((T, HIDDEN), dtype=torch.float32, device=ctx.device)
+    ctx._bind_stream()
+    check(lib().qf_moe_combine(ctx.h, T, _ptr(residual), _ptr(shared_out), _ptr(hit), _ptr(miss),
+                               _ptr(out)), ctx.h)
+    return out
+
+
+def grouped_ffn(ctx: MoEContext, layer: MoELayerWeights, x: torch.Tensor, idx: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Unweighted routed expert outputs of every position, fp32 [T * 8, 2048]:
+    row t * 8 + k = expert idx[t, k] applied to x_t (qf_moe_grouped_ffn)."""
+    _check_x(x)
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T * TOPK, HIDDEN), dtype=torch.float32, device=ctx.device)
+    n = C.c_size_t()
+    check(lib().qf_moe_grouped_ffn_workspace_size(ctx.h, T, C.byref(n)), ctx.h)
+    ws = torch.empty(n.value, dtype=torch.uint8, device=ctx.device)
+    ctx._bind_stream()
+    d = layer.desc()
+    check(lib().qf_moe_grouped_ffn(ctx.h, C.byref(d), T, _ptr(x), _ptr(idx), _ptr(out), _ptr(ws),
+                                   ws.numel()), ctx.h)
+    return out
+
+
 def block_forward_prenorm(ctx: MoEContext, layer: MoELayerWeights, hidden: torch.Tensor,
                           norm_w: torch.Tensor, eps: float = 1e-6, *, out: torch.Tensor | None = None,
                           return_routing: bool = False):

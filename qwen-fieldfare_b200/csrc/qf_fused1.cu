@@ -77,6 +77,7 @@ constexpr int kDnCols = kTopK + 1;               // down columns: 8 routed + sha
 constexpr int kItemsD = kDnCols * 4;             // (column, K-quarter) items of phase D
 
 struct Misc1 {
+  int pred[kTopK];  // predicted (or known) records of the next layer
   int idx[kTopK];
   float w[kTopK];
   int rec[kTopK];
@@ -107,7 +108,27 @@ constexpr int kOffRed = kOffAC + 8 * kDnCols * 4;
 constexpr int kRedFloats = kItemsD * 16 + 16;
 constexpr int kOffMisc = (kOffRed + kRedFloats * 4 + 127) & ~127;
 constexpr int kOffBar = (kOffMisc + (int)sizeof(Misc1) + 127) & ~127;
-constexpr int kNBars = 5;  // dib[2] (token-independent, by layer parity), rgu[2], rdn
+constexpr int kNBars = 6;  // dib[2] (token-independent, by layer parity), rgu[2], rdn, pred
+// Speculative prefetch of the next layer's routed records.  The CTAs past the
+// output tiles (b >= 128: no R task, no D phase, one routed gate/up tile)
+// predict layer l + 1's top-8 by applying layer l + 1's router to x_l (the
+// residual stream changes little from layer to layer: about 85% of the next
+// layer's experts are predicted on the synthetic 40-layer stack), once their
+// own gate/up tile of layer l is done, i.e. after the bulk of layer l's
+// routed fetch; they then prefetch the 8 predicted records (14.2 MB) into L2,
+// split among them, while HBM is otherwise idle (layer l's down phase, the
+// next prologue, router and top-8).  Layer l + 1's routed copies then hit L2
+// for the predicted experts.  With supplied routing (idx_in) the next layer's
+// records are known and prefetched exactly.  Results are unaffected: only
+// the prefetch is speculative.
+constexpr int kPredMinCtas = 16;                  // predictor CTAs needed (rows per CTA <= 16)
+constexpr int kPredMaxRows = kExperts / kPredMinCtas;
+constexpr int kPredRowBytes = 2048 + 2 * 64;      // codes + scales + biases of a router row
+constexpr int kOffPred = 2 * kGuTileBytes;        // inside the routed area: predictors use tile 0 only
+constexpr int kPredChunk = 16384;                 // L2 prefetch granule
+constexpr int kChunksPerRecord = static_cast<int>(kRecordBytes / kPredChunk);  // 108
+static_assert(kRecordBytes % kPredChunk == 0, "record = whole prefetch chunks");
+static_assert(kOffPred + kPredMaxRows * kPredRowBytes <= kRoutedBytes, "prediction rows fit");
 constexpr int kSmemBytes = kOffBar + kNBars * 8;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 static_assert(kOffXfrag % 16 == 0 && kOffAfrag % 16 == 0 && kOffRouted % 128 == 0, "alignment");
@@ -133,6 +154,7 @@ struct Fused1Args {
   uint64_t* ll_logits;  // [257]: router logits, then the shared-gate coefficient
   uint64_t* ll_act;     // [9 * 256]: fp16 pairs; rows 0..7 routed positions, 8 the shared expert
   uint64_t* ll_h;       // [2048 + 128]: block output, then the RMS partials of its row tiles
+  uint64_t* ll_pred;    // [256]: predicted logits of the next layer (tag = next layer + 1)
   int* status;
   LayerW layers[kMaxLayers];
 };
@@ -455,6 +477,105 @@ __device__ __forceinline__ void stage_f16(const __half* src, int nvec, int ngrp,
   }
 }
 
+// Predictor p's router rows [r0, r0 + n) of a layer: codes row-major, then
+// the scales, then the biases (64 bytes a row each); completion on `bar`.
+__device__ void issue_pred_rows(const LayerW& L, int r0, int n, unsigned char* buf, uint64_t* bar) {
+  int t0 = copy_block(buf, 2048, L.rw + static_cast<size_t>(r0) * 2048, 2048, n, 7, 0);
+  t0 = copy_block(buf + n * 2048, 64, reinterpret_cast<const uint8_t*>(L.rs + r0 * 32), 64, n, 2, t0);
+  copy_block(buf + n * 2048 + n * 64, 64, reinterpret_cast<const uint8_t*>(L.rb + r0 * 32), 64, n, 2, t0);
+  cp_async_arrive(bar);
+}
+
+// One predicted logit per warp (rows w, w + 16, ...): the router row dotted
+// with x (fp16) in the reference's per-lane order; only a prediction, so the
+// order is not load-bearing.
+template <bool BF16>
+__device__ void predict_rows(const unsigned char* buf, int n, const __half* xh, int lane, int warp,
+                             uint64_t* ll_pred, int r0, uint32_t tag) {
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(buf + n * 2048);
+  const uint16_t* bi = sc + n * 32;
+#pragma unroll 1
+  for (int w = warp; w < n; w += kWarps) {
+    float acc = 0.f;
+#pragma unroll 1
+    for (int blk = 0; blk < 8; blk++) {
+      const uint2 wv = *reinterpret_cast<const uint2*>(buf + w * 2048 + blk * 256 + lane * 8);
+      const uint4 hv = *reinterpret_cast<const uint4*>(xh + blk * 256 + lane * 8);
+      const __half2* h2 = reinterpret_cast<const __half2*>(&hv);
+      float d = 0.f, sm = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float2 xf = __half22float2(h2[k]);
+        const uint32_t wd = k < 2 ? wv.x : wv.y;
+        d = __fmaf_rn(byte_f(wd, (2 * k) & 3), xf.x, d);
+        d = __fmaf_rn(byte_f(wd, (2 * k + 1) & 3), xf.y, d);
+        sm = __fadd_rn(__fadd_rn(sm, xf.x), xf.y);
+      }
+      const int g = blk * 4 + (lane >> 3);
+      acc = __fmaf_rn(cvt16<BF16>(sc[w * 32 + g]), d, acc);
+      acc = __fmaf_rn(cvt16<BF16>(bi[w * 32 + g]), sm, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) ll_put(ll_pred + r0 + w, __float_as_uint(acc), tag);
+  }
+}
+
+// Warp 0 of a predictor: the 256 predicted logits (bounded wait; on expiry
+// the prefetch is skipped, nothing is reported: it is only a prefetch), the
+// top 8 of them (+ the harness bias), written to ex[8].  Returns false when
+// the logits did not all arrive.
+__device__ bool predict_top8(const uint64_t* ll_pred, uint32_t tag, const float* bias, int lane, int* ex) {
+  uint64_t v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] = ll_get(ll_pred + j * 32 + lane);
+#pragma unroll 1
+  for (unsigned round = 0;; round++) {
+    bool ready = true;
+#pragma unroll
+    for (int j = 0; j < 8; j++) ready &= static_cast<uint32_t>(v[j] >> 32) == tag;
+    if (__all_sync(0xffffffffu, ready)) break;
+    if (round > 4096) return false;  // a safety net only: the 256 words arrive within microseconds
+    __nanosleep(64);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (static_cast<uint32_t>(v[j] >> 32) != tag) v[j] = ll_get(ll_pred + j * 32 + lane);
+  }
+  uint32_t key[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    float lg = __uint_as_float(static_cast<uint32_t>(v[j]));
+    if (bias) lg = __fadd_rn(lg, __ldg(bias + j * 32 + lane));
+    key[j] = f2ord(lg);
+  }
+  uint32_t taken = 0;
+#pragma unroll 1
+  for (int k = 0; k < kTopK; k++) {
+    uint32_t best = 0, bj = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (!((taken >> j) & 1u) && key[j] >= best) {
+        best = key[j];
+        bj = static_cast<uint32_t>(j);
+      }
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t e = bj * 32u + static_cast<uint32_t>(lane);
+    const uint32_t win = __reduce_min_sync(0xffffffffu, best == mx ? e : 0xffffffffu);
+    if (static_cast<int>(win & 31u) == lane) taken |= 1u << (win >> 5);
+    if (lane == 0) ex[k] = static_cast<int>(win);
+  }
+  return true;
+}
+
+// Predictor p of np: L2 prefetch of its share of the 8 records' 16 KB chunks.
+__device__ void prefetch_records(const LayerW& L, const int* rec, int p, int np, int lane) {
+  for (int c = p + np * lane; c < kTopK * kChunksPerRecord; c += np * 32) {
+    const int k = c / kChunksPerRecord, q = c % kChunksPerRecord;
+    const int r = rec[k];
+    if (r < 0 || static_cast<uint32_t>(r) >= L.bank_records) continue;
+    prefetch_l2(L.bank + static_cast<uint64_t>(r) * L.stride + static_cast<size_t>(q) * kPredChunk, kPredChunk);
+  }
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ Fused1Args A) {
   extern __shared__ __align__(128) unsigned char sm[];
@@ -475,9 +596,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
   const int b = blockIdx.x, G = gridDim.x;
   const bool has_r = b < kNR, has_d = b < kNOut, has_di = has_r || has_d;
   const int n_gu = (b < kNGu ? 1 : 0) + (b + G < kNGu ? 1 : 0);
+  // predictor CTAs (see kPredMinCtas): p of np, router rows [pr0, pr0 + pn)
+  const int np = G - kNOut;
+  const bool is_pred = np >= kPredMinCtas && b >= kNOut && n_gu == 1;
+  const int pp = b - kNOut, prows = (kExperts + np - 1) / (np > 0 ? np : 1);
+  const int pr0 = is_pred ? pp * prows : 0;
+  const int pn = is_pred ? max(0, min(kExperts - pr0, prows)) : 0;
+  unsigned char* const pbuf = sm + kOffRouted + kOffPred;
   // Per mbarrier: phases completed so far (wait parity) and whether a phase is
   // armed and not yet waited for.  Uniform across the CTA.
-  uint32_t phase[kNBars] = {0, 0, 0, 0, 0};
+  uint32_t phase[kNBars] = {0, 0, 0, 0, 0, 0};
   uint32_t armed = 0;
 
   if (tid == 0) {
@@ -511,6 +639,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
       issue_di(A.layers[1], b, sm + kOffDi + kDiBytes, &bars[1]);
       armed |= 2u;
     }
+  }
+
+  if (is_pred && pn > 0 && !A.r.idx_in && A.n_layers > 1) {
+    issue_pred_rows(A.layers[1], pr0, pn, pbuf, &bars[5]);
+    armed |= 32u;
   }
 
   for (int li = 0; li < A.n_layers; li++) {
@@ -735,6 +868,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
         return;
       }
     }
+    // ---------------- predictors: the next layer's records into L2
+    if (is_pred && li + 1 < A.n_layers) {
+      const LayerW& Ln = A.layers[li + 1];
+      if (A.r.idx_in) {
+        if (tid < kTopK)
+          m->pred[tid] = A.r.rec_of_pos ? A.r.rec_of_pos[(size_t)(l + 1) * kTopK + tid]
+                                        : A.r.idx_in[(size_t)(l + 1) * kTopK + tid];
+        __syncthreads();
+        if (warp == 0) prefetch_records(Ln, m->pred, pp, np, lane);
+      } else {
+        wait_bar(5);
+        __syncthreads();
+        if (m->fail) {
+          drain();
+          return;
+        }
+        if (pn > 0) predict_rows<BF16>(pbuf, pn, xh, lane, warp, A.ll_pred, pr0, tag + 1u);
+        if (warp == 0 && predict_top8(A.ll_pred, tag + 1u, A.r.bias, lane, m->pred)) {
+          __syncwarp();
+          prefetch_records(Ln, m->pred, pp, np, lane);
+        }
+      }
+    }
     if (b == 0 && tid < kTopK) {
       if (A.idx_out) A.idx_out[(size_t)l * kTopK + tid] = m->idx[tid];
       if (A.w_out) A.w_out[(size_t)l * kTopK + tid] = m->w[tid];
@@ -811,6 +967,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused1(const __grid_constant__ 
       issue_di(A.layers[li + 2], b, di, &bars[par]);
       armed |= 1u << par;
     }
+    if (is_pred && pn > 0 && !A.r.idx_in && li + 2 < A.n_layers) {
+      issue_pred_rows(A.layers[li + 2], pr0, pn, pbuf, &bars[5]);
+      armed |= 32u;
+    }
   }
 }
 
@@ -822,7 +982,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 size_t fused1_workspace_bytes() {
   auto a = [](size_t n) { return (n + 255) & ~(size_t)255; };
-  return a(8 * (kExperts + 1)) + a(8 * kActWords) + a(8 * (kHidden + kNOut));
+  return a(8 * (kExperts + 1)) + a(8 * kActWords) + a(8 * (kHidden + kNOut)) + a(8 * kExperts);
 }
 
 cudaError_t fused1_init_attributes() {
@@ -881,6 +1041,7 @@ cudaError_t fused1_stack(cudaStream_t st, const LayerW* layers, int n_layers, bo
   A.ll_logits = reinterpret_cast<uint64_t*>(take(8 * (kExperts + 1)));
   A.ll_act = reinterpret_cast<uint64_t*>(take(8 * kActWords));
   A.ll_h = reinterpret_cast<uint64_t*>(take(8 * (kHidden + kNOut)));
+  A.ll_pred = reinterpret_cast<uint64_t*>(take(8 * kExperts));
   const size_t ll_bytes = static_cast<size_t>(p - reinterpret_cast<char*>(A.ll_logits));
   // tags restart at 1 every call: clear the words of the previous call
   e = cudaMemsetAsync(A.ll_logits, 0, ll_bytes, st);

@@ -168,24 +168,43 @@ __device__ __forceinline__ float h16_to_f32(uint16_t u) {
 // accumulates dot = fma-chain of 8 products, acc = fma(s, dot, acc),
 // acc = fma(b, xsum, acc); the lanes are then summed with the xor butterfly
 // 16, 8, 4, 2, 1 (simd_sum), so the logits are bit-identical to the decode
-// router and the oracle.  A CTA computes 32 router rows x 8 tokens: each warp
-// holds 4 rows' codes of the current block in registers (converted once) and
-// streams the 8 tokens' x slices from shared memory, where x is staged once
-// per CTA as fp32 (exact widening of the fp16 input), so every 32-byte read
-// of x (8 wavefronts) and of its 8-value sum (1 wavefront) feeds 4 rows x 10
-// FMAs.  In shared memory the two 16-byte halves of 8-element group c are
-// swapped when bit 2 of c is set, so the eight lanes of a quarter-warp (32
-// bytes apart) read distinct banks.  The last row of CTAs (blockIdx.y == 8)
+// router and the oracle.  A CTA computes 32 router rows x 8 tokens (4 rows
+// per warp).  The two chains of a token pair run together in Blackwell's
+// packed fp32 FMA (fma.rn.f32x2: each half rounded as a scalar fma, so every
+// logit is bit-identical to the scalar chain): x is staged once per CTA as
+// fp32 pairs {x_t, x_t+1} laid out [pair][block][element][lane] (a warp's
+// 8-byte reads of one element are 256 contiguous bytes), each code byte
+// becomes an exact {q, q} pair (byte into the 2^23 mantissa, one packed
+// subtract), and the element loop runs outermost so that 4 rows x 4 pairs of
+// dot chains stay in registers.  The last row of CTAs (blockIdx.y == 8)
 // computes the shared-gate coefficient instead, one lane per token, as the
 // reference's single sequential chain (qwen_gemv_q8_affine,
 // deltanet.metal:863-902).
 constexpr int kRtTok = 8;
+constexpr int kRtPairs = kRtTok / 2;
 constexpr int kRtWarps = 8;
 constexpr int kRtRowsPerWarp = 4;
 constexpr int kRtRows = kRtWarps * kRtRowsPerWarp;  // 32 router rows per CTA
 constexpr int kRtThreads = kRtWarps * 32;
 constexpr int kRtRowBlocks = kExperts / kRtRows;  // + 1 row of coefficient CTAs
-constexpr size_t kRtSmem = sizeof(float) * (kRtTok * kHidden + kRtTok * 256);
+constexpr size_t kRtSmem = sizeof(uint64_t) * (kRtPairs * kHidden + kRtPairs * 256);
+
+__device__ __forceinline__ uint64_t rt_pk(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ uint64_t rt_fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// {q, q} of byte k of w, exact: (2^23 + q) - 2^23 in both halves
+__device__ __forceinline__ uint64_t rt_byte2(uint32_t w, int k) {
+  const uint32_t u = 0x4B000000u | ((w >> (8 * k)) & 0xFFu);
+  const uint64_t m = (uint64_t)u | ((uint64_t)u << 32);
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(m), "l"(0xCB000000CB000000ull));
+  return d;
+}
 
 template <bool BF16>
 __global__ void __launch_bounds__(kRtThreads, 2) k_router_prefill(LayerW L, int T,
@@ -193,43 +212,52 @@ __global__ void __launch_bounds__(kRtThreads, 2) k_router_prefill(LayerW L, int 
                                                                   float* __restrict__ logits,
                                                                   float* __restrict__ coef) {
   extern __shared__ float4 rsm4[];
-  float* xs = reinterpret_cast<float*>(rsm4);  // [8][2048], group halves swizzled
-  float* xsum = xs + kRtTok * kHidden;         // [8][8 blk][32 lanes]
+  uint64_t* xs2 = reinterpret_cast<uint64_t*>(rsm4);  // [pair][8 blk][8 k][32 lanes]
+  uint64_t* xsum2 = xs2 + kRtPairs * kHidden;         // [pair][8 blk][32 lanes]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * kRtTok;
   const int tn = min(kRtTok, T - t0);
-  // x rows (zero past the last token) and the in-order sum of every 8-value group
-  for (int i = tid; i < kRtTok * (kHidden / 8); i += kRtThreads) {
-    const int t = i / (kHidden / 8), c = i % (kHidden / 8);
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (t < tn) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
-    const __half2* h = reinterpret_cast<const __half2*>(&v);
-    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), cc = __half22float2(h[2]),
-                 dd = __half22float2(h[3]);
-    float4* d = reinterpret_cast<float4*>(xs + t * kHidden + c * 8);
-    const int sw = (c >> 2) & 1;
-    d[sw] = make_float4(a.x, a.y, b.x, b.y);
-    d[sw ^ 1] = make_float4(cc.x, cc.y, dd.x, dd.y);
-    float sm = a.x;
-    sm = __fadd_rn(sm, a.y);
-    sm = __fadd_rn(sm, b.x);
-    sm = __fadd_rn(sm, b.y);
-    sm = __fadd_rn(sm, cc.x);
-    sm = __fadd_rn(sm, cc.y);
-    sm = __fadd_rn(sm, dd.x);
-    sm = __fadd_rn(sm, dd.y);
-    xsum[i] = sm;  // i = t * 256 + blk * 32 + lane
+  // item = (pair, 8-element group c = blk * 32 + lane): both tokens' 8 values
+  for (int i = tid; i < kRtPairs * (kHidden / 8); i += kRtThreads) {
+    const int tp = i / (kHidden / 8), c = i % (kHidden / 8);
+    float v[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int t = 2 * tp + h;
+      uint4 u = make_uint4(0u, 0u, 0u, 0u);
+      if (t < tn) u = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
+      const __half2* hh = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 f = __half22float2(hh[j]);
+        v[h][2 * j] = f.x;
+        v[h][2 * j + 1] = f.y;
+      }
+    }
+    const int blk = c >> 5, ln = c & 31;
+    uint64_t* d = xs2 + ((size_t)(tp * 8 + blk) * 8) * 32 + ln;
+    float sm[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      float a = v[h][0];
+#pragma unroll
+      for (int k = 1; k < 8; k++) a = __fadd_rn(a, v[h][k]);
+      sm[h] = a;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) d[k * 32] = rt_pk(v[0][k], v[1][k]);
+    xsum2[(tp * 8 + blk) * 32 + ln] = rt_pk(sm[0], sm[1]);
   }
   __syncthreads();
   if (blockIdx.y < kRtRowBlocks) {
     constexpr int R = kRtRowsPerWarp;
     const int rbase = blockIdx.y * kRtRows + warp * R;
     const uint8_t* wrow = L.rw + (size_t)rbase * kHidden + lane * 8;
-    float acc[R][kRtTok];
+    uint64_t acc[R][kRtPairs];
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
-      for (int t = 0; t < kRtTok; t++) acc[r][t] = 0.f;
+      for (int p = 0; p < kRtPairs; p++) acc[r][p] = 0ull;
     uint2 wn[R];
     uint16_t sn[R], bn[R];
     auto fetch = [&](int blk) {
@@ -244,62 +272,71 @@ __global__ void __launch_bounds__(kRtThreads, 2) k_router_prefill(LayerW L, int 
     fetch(0);
 #pragma unroll 1
     for (int blk = 0; blk < 8; blk++) {
-      float q[R][8], sc[R], bi[R];
+      uint2 w[R];
+      uint64_t sc[R], bi[R];
 #pragma unroll
       for (int r = 0; r < R; r++) {
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-          q[r][k] = byte_f(wn[r].x, k);
-          q[r][4 + k] = byte_f(wn[r].y, k);
-        }
-        sc[r] = h16_to_f32<BF16>(sn[r]);
-        bi[r] = h16_to_f32<BF16>(bn[r]);
+        w[r] = wn[r];
+        const float s1 = h16_to_f32<BF16>(sn[r]), b1 = h16_to_f32<BF16>(bn[r]);
+        sc[r] = rt_pk(s1, s1);
+        bi[r] = rt_pk(b1, b1);
       }
       if (blk + 1 < 8) fetch(blk + 1);
-      const int sw = (lane >> 2) & 1;
+      uint64_t dot[R][kRtPairs];
 #pragma unroll
-      for (int t = 0; t < kRtTok; t++) {
-        const float4* e4 = reinterpret_cast<const float4*>(xs + t * kHidden + blk * 256 + lane * 8);
-        const float4 a = e4[sw], b = e4[sw ^ 1];
-        const float xsm = xsum[t * 256 + blk * 32 + lane];
+      for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int p = 0; p < kRtPairs; p++) dot[r][p] = 0ull;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        uint64_t xv[kRtPairs];
+#pragma unroll
+        for (int p = 0; p < kRtPairs; p++) xv[p] = xs2[((size_t)(p * 8 + blk) * 8 + k) * 32 + lane];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-          float dot = 0.f;
-          dot = __fmaf_rn(q[r][0], a.x, dot);
-          dot = __fmaf_rn(q[r][1], a.y, dot);
-          dot = __fmaf_rn(q[r][2], a.z, dot);
-          dot = __fmaf_rn(q[r][3], a.w, dot);
-          dot = __fmaf_rn(q[r][4], b.x, dot);
-          dot = __fmaf_rn(q[r][5], b.y, dot);
-          dot = __fmaf_rn(q[r][6], b.z, dot);
-          dot = __fmaf_rn(q[r][7], b.w, dot);
-          acc[r][t] = __fmaf_rn(bi[r], xsm, __fmaf_rn(sc[r], dot, acc[r][t]));
+          const uint64_t q2 = rt_byte2(k < 4 ? w[r].x : w[r].y, k & 3);
+#pragma unroll
+          for (int p = 0; p < kRtPairs; p++) dot[r][p] = rt_fma2(q2, xv[p], dot[r][p]);
         }
+      }
+#pragma unroll
+      for (int p = 0; p < kRtPairs; p++) {
+        const uint64_t xsm = xsum2[(p * 8 + blk) * 32 + lane];
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r][p] = rt_fma2(bi[r], xsm, rt_fma2(sc[r], dot[r][p], acc[r][p]));
       }
     }
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
-      for (int t = 0; t < kRtTok; t++) {
-        const float v = warp_sum(acc[r][t]);
-        if (lane == ((r * kRtTok + t) & 31) && t < tn) logits[(size_t)(t0 + t) * kExperts + rbase + r] = v;
-      }
+      for (int p = 0; p < kRtPairs; p++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int t = 2 * p + h;
+          const float v = warp_sum(__uint_as_float((uint32_t)(acc[r][p] >> (32 * h))));
+          if (lane == ((r * kRtTok + t) & 31) && t < tn) logits[(size_t)(t0 + t) * kExperts + rbase + r] = v;
+        }
   } else if (coef && warp == 0) {
     const int t = lane;
     if (t < tn) {
-      const float* xt = xs + t * kHidden;
+      const int tp = t >> 1, h = t & 1;
+      // x_t[e], e = c * 8 + k, c = blk * 32 + ln
+      auto xe = [&](int e) {
+        const int c = e >> 3, k = e & 7;
+        const uint64_t pr = xs2[((size_t)(tp * 8 + (c >> 5)) * 8 + k) * 32 + (c & 31)];
+        return __uint_as_float((uint32_t)(pr >> (32 * h)));
+      };
       float acc = 0.f;
       for (int g = 0; g < kHidden / kGroup; g++) {
         const float sc = ld16<BF16>(L.cs, g), bi = ld16<BF16>(L.cb, g);
 #pragma unroll 4
         for (int u = 0; u < 16; u++) {
           const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(L.cw + g * 64) + u);
-          const int c = g * 8 + (u >> 1);  // 8-element group
-          const float4 xv = *reinterpret_cast<const float4*>(xt + c * 8 + (((u & 1) ^ ((c >> 2) & 1)) << 2));
-          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 0), sc, bi), xv.x, acc);
-          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 1), sc, bi), xv.y, acc);
-          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 2), sc, bi), xv.z, acc);
-          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 3), sc, bi), xv.w, acc);
+          const int e = g * 64 + u * 4;
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 0), sc, bi), xe(e), acc);
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 1), sc, bi), xe(e + 1), acc);
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 2), sc, bi), xe(e + 2), acc);
+          acc = __fmaf_rn(__fmaf_rn(byte_f(wv, 3), sc, bi), xe(e + 3), acc);
         }
       }
       coef[t0 + t] = acc;

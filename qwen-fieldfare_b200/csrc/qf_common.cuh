@@ -166,4 +166,30 @@ __device__ __forceinline__ void topk_token(int t, const float* __restrict__ logi
   }
 }
 
+// Exclusive prefix sum of v over threads 0..255 of the block (threads past 255
+// pass 0 and get their own running prefix, which callers ignore); *total is
+// the sum over the 256.  Every thread of the block calls it (it contains a
+// barrier); s_warp: 8 ints of shared memory, free again after the next
+// barrier.
+__device__ __forceinline__ int block_scan256(int v, int* s_warp, int* total) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int incl = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += o;
+  }
+  if (tid < 256 && lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int before = 0, tot = 0;
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    const int sw = s_warp[q];
+    if (q < warp) before += sw;
+    tot += sw;
+  }
+  *total = tot;
+  return before + incl - v;
+}
+
 }  // namespace qf

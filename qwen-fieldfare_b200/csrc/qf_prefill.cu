@@ -176,10 +176,11 @@ __device__ __forceinline__ float h16_to_f32(uint16_t u) {
 // 8-byte reads of one element are 256 contiguous bytes), each code byte
 // becomes an exact {q, q} pair (byte into the 2^23 mantissa, one packed
 // subtract), and the element loop runs outermost so that 4 rows x 4 pairs of
-// dot chains stay in registers.  The last row of CTAs (blockIdx.y == 8)
+// dot chains stay in registers.  One row of CTAs
 // computes the shared-gate coefficient instead, one lane per token, as the
 // reference's single sequential chain (qwen_gemv_q8_affine,
-// deltanet.metal:863-902).
+// deltanet.metal:863-902); that row is blockIdx.y == 0, so its long chains
+// start in the first wave instead of trailing the grid.
 constexpr int kRtTok = 8;
 constexpr int kRtPairs = kRtTok / 2;
 constexpr int kRtWarps = 8;
@@ -217,15 +218,30 @@ __global__ void __launch_bounds__(kRtThreads, 2) k_router_prefill(LayerW L, int 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * kRtTok;
   const int tn = min(kRtTok, T - t0);
-  // item = (pair, 8-element group c = blk * 32 + lane): both tokens' 8 values
-  for (int i = tid; i < kRtPairs * (kHidden / 8); i += kRtThreads) {
+  // item = (pair, 8-element group c = blk * 32 + lane): both tokens' 8 values;
+  // every load of the thread's items is issued before the first is used
+  constexpr int kItems = kRtPairs * (kHidden / 8) / kRtThreads;  // 4 per thread
+  static_assert(kItems * kRtThreads == kRtPairs * (kHidden / 8), "items per thread");
+  uint4 ld[kItems][2];
+#pragma unroll
+  for (int it = 0; it < kItems; it++) {
+    const int i = tid + it * kRtThreads;
+    const int tp = i / (kHidden / 8), c = i % (kHidden / 8);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int t = 2 * tp + h;
+      ld[it][h] = t < tn ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c)
+                         : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < kItems; it++) {
+    const int i = tid + it * kRtThreads;
     const int tp = i / (kHidden / 8), c = i % (kHidden / 8);
     float v[2][8];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-      const int t = 2 * tp + h;
-      uint4 u = make_uint4(0u, 0u, 0u, 0u);
-      if (t < tn) u = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * kHidden) + c);
+      const uint4 u = ld[it][h];
       const __half2* hh = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
       for (int j = 0; j < 4; j++) {
@@ -249,9 +265,9 @@ __global__ void __launch_bounds__(kRtThreads, 2) k_router_prefill(LayerW L, int 
     xsum2[(tp * 8 + blk) * 32 + ln] = rt_pk(sm[0], sm[1]);
   }
   __syncthreads();
-  if (blockIdx.y < kRtRowBlocks) {
+  if (blockIdx.y > 0) {
     constexpr int R = kRtRowsPerWarp;
-    const int rbase = blockIdx.y * kRtRows + warp * R;
+    const int rbase = (blockIdx.y - 1) * kRtRows + warp * R;
     const uint8_t* wrow = L.rw + (size_t)rbase * kHidden + lane * 8;
     uint64_t acc[R][kRtPairs];
 #pragma unroll
@@ -436,6 +452,7 @@ __global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
   __shared__ int wh[kPlanSmallThreads / 32][kExperts];  // per-warp counts, then prefix
   __shared__ int s_rem[kListThreads];
   __shared__ int s_warp[kListThreads / 32];
+  __shared__ int s_scan[kExperts / 32];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = T * kTopK;
   if (idx_in) {
@@ -447,8 +464,9 @@ __global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
     if (warp < T) topk_token(warp, logits, bias, idx, w, lane);
   }
   __syncthreads();
+  const int nw = (n + 31) >> 5;  // warps that hold positions
   for (int i = tid; i < kExperts; i += blockDim.x) h[i] = 0;
-  for (int i = tid; i < (kPlanSmallThreads / 32) * kExperts; i += blockDim.x) (&wh[0][0])[i] = 0;
+  for (int i = tid; i < nw * kExperts; i += blockDim.x) (&wh[0][0])[i] = 0;
   __syncthreads();
   int e = -1;
   if (tid < n) {
@@ -467,17 +485,15 @@ __global__ void __launch_bounds__(kPlanSmallThreads) k_plan_small(
   const int rank = __popc(peers & ((1u << lane) - 1u));
   if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) wh[warp][e] = __popc(peers);
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int i = 0; i < kExperts; i++) {
-      excl[i] = acc;
-      acc += h[i];
-    }
-    excl[kExperts] = acc;
+  {
+    int total = 0;
+    const int ex = block_scan256(tid < kExperts ? h[tid] : 0, s_scan, &total);
+    if (tid < kExperts) excl[tid] = ex;
+    if (tid == 0) excl[kExperts] = total;
   }
   for (int x = tid; x < kExperts; x += blockDim.x) {
     int acc = 0;
-    for (int q = 0; q < kPlanSmallThreads / 32; q++) {
+    for (int q = 0; q < nw; q++) {
       const int c = wh[q][x];
       wh[q][x] = acc;
       acc += c;
@@ -1120,7 +1136,8 @@ cudaError_t prefill_init_attributes() {
 
 cudaError_t router_logits_prefill(cudaStream_t st, const LayerW& L, bool bf16, int T,
                                   const uint16_t* x, float* logits, float* coef) {
-  const dim3 grid((T + kRtTok - 1) / kRtTok, kRtRowBlocks + (coef ? 1 : 0));
+  // blockIdx.y == 0: the coefficient CTAs (no work when coef is NULL)
+  const dim3 grid((T + kRtTok - 1) / kRtTok, kRtRowBlocks + 1);
   if (bf16)
     k_router_prefill<true><<<grid, kRtThreads, kRtSmem, st>>>(L, T, x, logits, coef);
   else

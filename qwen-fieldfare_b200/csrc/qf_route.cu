@@ -41,26 +41,16 @@ __global__ void __launch_bounds__(kExperts) k_plan_scan(int n_chunks, const int*
                                                          int* __restrict__ chunk_offsets,
                                                          int* __restrict__ counts,
                                                          int* __restrict__ offsets) {
-  __shared__ int tot[kExperts];
-  __shared__ int excl[kExperts + 1];
+  __shared__ int s_warp[kExperts / 32];
   const int e = threadIdx.x;
   int s = 0;
   for (int c = 0; c < n_chunks; c++) s += chunk_counts[c * kExperts + e];
-  tot[e] = s;
-  __syncthreads();
-  if (e == 0) {
-    int acc = 0;
-    for (int i = 0; i < kExperts; i++) {
-      excl[i] = acc;
-      acc += tot[i];
-    }
-    excl[kExperts] = acc;
-  }
-  __syncthreads();
-  counts[e] = tot[e];
-  offsets[e] = excl[e];
-  if (e == 0) offsets[kExperts] = excl[kExperts];
-  int run = excl[e];
+  int total = 0;
+  const int ex = block_scan256(s, s_warp, &total);
+  counts[e] = s;
+  offsets[e] = ex;
+  if (e == 0) offsets[kExperts] = total;
+  int run = ex;
   for (int c = 0; c < n_chunks; c++) {
     chunk_offsets[c * kExperts + e] = run;
     run += chunk_counts[c * kExperts + e];

@@ -8,11 +8,14 @@
 //   dispatch  one kernel publishes this rank's per-expert counts into every
 //             rank's count board, waits until all ranks have published (which
 //             also means every rank has finished reading the previous call's
-//             buffers), and stores each routed token row (fp16, already in the
-//             grouped GEMM's K order) straight into the owner's receive rows
-//             over NVLink: rows land expert-major, then by source rank, then in
-//             the source's (token, k) order, so the owner's grouped GEMM reads
-//             contiguous rows of its own memory;
+//             buffers), and stores each token row (fp16, already in the grouped
+//             GEMM's K order) over NVLink ONCE per owner rank that holds any of
+//             its 8 experts, into the owner's token area (row source rank x
+//             max_tokens + token); each routed row sends only the 4-byte index
+//             of that token row to its receive row, which lands expert-major,
+//             then by source rank, then in the source's (token, k) order;
+//   expand    the owner copies the token rows into its receive rows (local
+//             HBM), so its grouped GEMM reads contiguous rows of its own memory;
 //   GEMMs     the owner runs the grouped tcgen05 gate/up and down GEMMs over
 //             its received rows plus its own tokens' shared-expert rows; the
 //             down GEMM's epilogue stores each fp32 result row straight into the
@@ -101,6 +104,9 @@ struct EpArgs {
   uint8_t* peer[kMaxRanks];  // exported region of each rank (this rank's own included)
   size_t x_off, y_off;   // receive rows / result rows inside a region
   size_t ret_off;        // int [rows_cap]: return address of each received row
+  size_t tok_off;        // token area: [world][t_max] fp16 rows, one per (source rank, token)
+  size_t src_off;        // int [rows_cap]: token-area row of each received routed row
+  int t_max;             // tokens per rank of the token area
   int pmax;              // result rows [0, pmax) are send rows, [pmax, pmax + T) shared rows
   int* loc_of_pos;       // [P] send row of each position (its result row here)
   int* counts_local;     // [256] received rows per local expert (zero past epr)
@@ -196,6 +202,7 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
   const int n_rows = a.P + a.T;
   for (int j = blockIdx.x * (kDispThreads / 32) + warp; j < n_rows; j += gridDim.x * (kDispThreads / 32)) {
     int src_t, d, row;
+    uint4* dst;
     if (j < a.P) {
       const int pos = a.perm[j];
       const int e = a.idx[pos];
@@ -210,20 +217,39 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
       d = e / a.epr;
       row = s_base[e] + (j - a.offsets[e]);
       if (lane == 0) a.loc_of_pos[pos] = j;
+      if (row < 0 || row >= a.rows_cap || src_t >= a.t_max) {
+        if (lane == 0) set_status(a.status, kStatusDevice);
+        continue;
+      }
+      const int trow = a.rank * a.t_max + src_t;
+      if (lane == 0) {
+        // where the owner's down GEMM sends this row's result, and which
+        // token row the owner expands into it
+        reinterpret_cast<int*>(a.peer[d] + a.ret_off)[row] = (a.rank << 24) | j;
+        reinterpret_cast<int*>(a.peer[d] + a.src_off)[row] = trow;
+      }
+      // the token row crosses once per owner: sent by the token's first
+      // position (lowest k) with an expert on that owner
+      bool first = true;
+      const int k = pos & 7;
+      for (int kk = 0; kk < k; kk++) {
+        const int e2 = a.idx[(src_t << 3) + kk];
+        first &= !(e2 >= 0 && e2 < kExperts && e2 / a.epr == d);
+      }
+      if (!first) continue;
+      dst = reinterpret_cast<uint4*>(a.peer[d] + a.tok_off) + static_cast<size_t>(trow) * (kHidden / 8);
     } else {
       d = a.rank;
       src_t = j - a.P;
       row = s_q + src_t;
+      if (row < 0 || row >= a.rows_cap) {
+        if (lane == 0) set_status(a.status, kStatusDevice);
+        continue;
+      }
+      if (lane == 0) reinterpret_cast<int*>(a.peer[d] + a.ret_off)[row] = (a.rank << 24) | (a.pmax + src_t);
+      dst = reinterpret_cast<uint4*>(a.peer[d] + a.x_off) + static_cast<size_t>(row) * (kHidden / 8);
     }
-    if (row < 0 || row >= a.rows_cap) {
-      if (lane == 0) set_status(a.status, kStatusDevice);
-      continue;
-    }
-    // where the owner's down GEMM sends this row's result
-    if (lane == 0)
-      reinterpret_cast<int*>(a.peer[d] + a.ret_off)[row] = (a.rank << 24) | (j < a.P ? j : a.pmax + src_t);
     const uint4* s = a.x + static_cast<size_t>(src_t) * (kHidden / 8);
-    uint4* dst = reinterpret_cast<uint4*>(a.peer[d] + a.x_off) + static_cast<size_t>(row) * (kHidden / 8);
     uint4 vv[kHidden / 8 / 32];
 #pragma unroll
     for (int q = 0; q < kHidden / 8 / 32; q++) vv[q] = __ldg(s + lane + 32 * q);
@@ -245,6 +271,30 @@ __global__ void k_ep_wait_rows(uint8_t* mine, unsigned target, const int* q_rows
   if (threadIdx.x == 0 && *(volatile const int*)q_rows >= 0 &&
       !wait_counter(sig(mine, kSigDelivered), target, wait_ns))
     set_status(status, kStatusTimeout);
+}
+
+// Owner: receive row r < q_rows (routed) <- its token-area row (local copy,
+// one warp per row).  Nothing after an expired wait (q_rows < 0).
+__global__ void __launch_bounds__(256) k_ep_expand(uint8_t* mine, size_t x_off, size_t tok_off, size_t src_off,
+                                                   int tok_rows, const int* q_rows, int* status) {
+  const int q = *q_rows;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int* src = reinterpret_cast<const int*>(mine + src_off);
+  const uint4* tok = reinterpret_cast<const uint4*>(mine + tok_off);
+  uint4* rows = reinterpret_cast<uint4*>(mine + x_off);
+  for (int r = warp; r < q; r += nw) {
+    const int t = __ldcg(src + r);
+    if (t < 0 || t >= tok_rows) {
+      if (lane == 0) set_status(status, kStatusDevice);
+      continue;
+    }
+    uint4 v[kHidden / 8 / 32];
+#pragma unroll
+    for (int i = 0; i < kHidden / 8 / 32; i++) v[i] = __ldcg(tok + static_cast<size_t>(t) * (kHidden / 8) + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < kHidden / 8 / 32; i++) rows[static_cast<size_t>(r) * (kHidden / 8) + lane + 32 * i] = v[i];
+  }
 }
 
 // The owner's result rows are written: tell every rank.
@@ -317,7 +367,7 @@ size_t al256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 struct qf_ep {
   qf_moe* h = nullptr;
   int device = 0, rank = 0, world = 1, epr = 256, t_max = 0, sms = 0;
-  size_t rows_cap = 0, region_bytes = 0, x_off = 0, y_off = 0, ret_off = 0, max_tiles = 0;
+  size_t rows_cap = 0, region_bytes = 0, x_off = 0, y_off = 0, ret_off = 0, tok_off = 0, src_off = 0, max_tiles = 0;
   uint8_t* region = nullptr;
   uint8_t* peer[qf::kMaxRanks] = {};
   bool opened[qf::kMaxRanks] = {};
@@ -384,7 +434,9 @@ qf_status qf_ep_create(qf_moe* h, int32_t rank, int32_t world, int32_t max_token
   ep->x_off = qf::kSigBytes;
   ep->y_off = ep->x_off + al256(ep->rows_cap * qf::kHidden * 2);
   ep->ret_off = ep->y_off + al256(ep->rows_cap * qf::kHidden * 4);
-  ep->region_bytes = ep->ret_off + al256(ep->rows_cap * 4);
+  ep->src_off = ep->ret_off + al256(ep->rows_cap * 4);
+  ep->tok_off = ep->src_off + al256(ep->rows_cap * 4);
+  ep->region_bytes = ep->tok_off + al256(static_cast<size_t>(world) * max_tokens * qf::kHidden * 2);
   ep->max_tiles = qf::grouped_max_tiles(max_tokens * world);
   size_t wsb = 0;
   wsb += al256(4 * (size_t)max_tokens * qf::kExperts) + al256(4 * (size_t)max_tokens);
@@ -535,6 +587,9 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   a.x_off = ep->x_off;
   a.y_off = ep->y_off;
   a.ret_off = ep->ret_off;
+  a.tok_off = ep->tok_off;
+  a.src_off = ep->src_off;
+  a.t_max = ep->t_max;
   a.pmax = ep->t_max * qf::kTopK;
   a.loc_of_pos = ep->loc_of_pos;
   a.counts_local = ep->counts_local;
@@ -548,6 +603,8 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
     qf::k_ep_dispatch<<<qf::kDispBlocks, qf::kDispThreads, 0, st>>>(a);
     qf::k_ep_wait_rows<<<1, 32, 0, st>>>(ep->region, a.epoch * (unsigned)ep->world * qf::kDispBlocks, ep->q_rows,
                                          h->d_status, ep->wait_ns);
+    qf::k_ep_expand<<<2 * ep->sms, 256, 0, st>>>(ep->region, ep->x_off, ep->tok_off, ep->src_off,
+                                                 ep->world * ep->t_max, ep->q_rows, h->d_status);
   }
   e = cudaGetLastError();
   if (e == cudaSuccess) e = qf::tile_list(st, ep->counts_local, ep->offsets_local, T, ep->q_rows, ep->tiles, ep->n_tiles);

@@ -653,11 +653,16 @@ def main():
 
     def measure_ep(T_total: int, steps: int, warmup: int):
         """one MoE block over T_total tokens split evenly over
-        the ranks, routed experts sharded 256/world per GPU, uniform-random top-8
-        (seeded), rows exchanged by the EP kernels over NVLink."""
+        the ranks, routed experts' gate/up sharded 256/world per GPU, uniform-random
+        top-8 (seeded), rows exchanged by the EP kernels over NVLink.  Timed in
+        both modes: down-at-home (the headline: owners return fp16 activation rows,
+        each rank runs the down projection of its own tokens with all 256 experts)
+        and fully sharded (owners also run the down projection and return fp32
+        result rows)."""
         T = T_total // world
         ep = Q.ExpertParallel(ctx, rank, world, max_tokens=T)
         local = ep.local_layer(0, 0)
+        full = layers[0]
         rng = np.random.default_rng(5000 + rank)
         idx = np.argsort(rng.random((T, 256)), axis=1)[:, :8].astype(np.int32)
         w = rng.random((T, 8)).astype(np.float32) + 0.05
@@ -666,42 +671,55 @@ def main():
         w_d = torch.from_numpy(w).to(dev)
         xs = [Q.synth_hidden(4000 + rank, i * T, T).to(dev) for i in range(2)]
         out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
-        for i in range(warmup):
-            ep.forward(local, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
-        ctx.check()
-        barrier()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        ev0.record()
-        for i in range(steps):
-            ep.forward(local, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
-        ev1.record()
-        ev1.synchronize()
-        ms = ev0.elapsed_time(ev1) / steps
-        barrier()
-        ms_max = max_over_ranks(ms)
+
+        def timed(dah: bool) -> float:
+            ep.set_down_at_home(dah)
+            lay = full if dah else local
+            for i in range(warmup):
+                ep.forward(lay, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
+            ctx.check()
+            barrier()
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            for i in range(steps):
+                ep.forward(lay, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
+            ev1.record()
+            ev1.synchronize()
+            ms = ev0.elapsed_time(ev1) / steps
+            barrier()
+            return max_over_ranks(ms)
+
+        ms_sharded = timed(False)
+        ms_max = timed(True)  # down-at-home, the headline; the breakdown below is of it
         kernels = {}
         for name in ("router", "dispatch", "gate_up", "down", "combine"):
             Q.profile_begin(ctx, name, 64)
             for i in range(6):
-                ep.forward(local, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
+                ep.forward(full, xs[i % 2], topk_idx=idx_d, topk_w=w_d, out=out)
             tot, n = Q.profile_end(ctx)
             kernels[name] = max_over_ranks(tot / max(n, 1))
         ctx.check()
-        # routed rows this rank sends to other ranks (4 KB each) and receives
+        # token rows this rank sends to other ranks (4 KB each, once per owner)
+        # and routed rows whose results come back (1 KB activations here, 8 KB
+        # fp32 rows in the sharded mode)
         owner = idx // ep.experts_per_rank
-        sent_remote = int((owner != rank).sum())
+        sent_remote = sum(len(set(o.tolist()) - {rank}) for o in owner)
+        routed_remote = int((owner != rank).sum())
         # correctness at this world size: every rank's EP output for all of its
         # tokens against the single-GPU block (all 256 experts resident on this
         # GPU, same tokens, same routing), bit for bit; min over ranks
         equal = True
         for k in range(2):
-            got = ep.forward(local, xs[k], topk_idx=idx_d, topk_w=w_d, out=out).clone()
             ref = Q.block_forward(ctx, layers[0], xs[k], topk_idx=idx_d, topk_w=w_d)
-            torch.cuda.synchronize()
-            equal = equal and bool(torch.equal(got, ref))
+            for dah in (True, False):  # both modes, the same reference
+                ep.set_down_at_home(dah)
+                got = ep.forward(full if dah else ep.local_layer(0, 0), xs[k], topk_idx=idx_d, topk_w=w_d,
+                                 out=out).clone()
+                torch.cuda.synchronize()
+                equal = equal and bool(torch.equal(got, ref))
         ctx.check()
-        flag = torch.tensor([1 if equal else 0, T * 2], dtype=torch.int64, device=dev)
+        flag = torch.tensor([1 if equal else 0, T * 4], dtype=torch.int64, device=dev)
         if dist is not None:
             f_min = flag[:1].clone()
             dist.all_reduce(f_min, op=dist.ReduceOp.MIN)
@@ -735,9 +753,12 @@ def main():
         tps1 = T_total / (ms1 / 1e3)
         return {"T_total": T_total, "T_rank": T, "ms_per_block": ms_max,
                 "tokens_per_s": tps, "kernel_ms": kernels,
+                "sharded_ms_per_block": ms_sharded, "sharded_tokens_per_s": T_total / (ms_sharded / 1e3),
                 "gemm_flops_per_rank": (routed + shared) / world,
                 "remote_rows_sent_rank0": sent_remote,
                 "dispatch_remote_bytes_rank0": sent_remote * 4096,
+                "return_remote_bytes_rank0": routed_remote * 1024,
+                "sharded_return_remote_bytes_rank0": routed_remote * 8192,
                 "ep_equal": bool(flag[0].item() == 1), "ep_checked_tokens": int(flag[1].item()),
                 "one_gpu_ms_per_block": ms1, "one_gpu_tokens_per_s": tps1,
                 "efficiency_vs_one_gpu": tps / (world * tps1)}
@@ -779,17 +800,23 @@ def main():
         gemm_ms = r["kernel_ms"]["gate_up"] + r["kernel_ms"]["down"]
         tf = r["gemm_flops_per_rank"] / (gemm_ms / 1e3) / 1e12
         return {
-            "workload": f"one MoE block over {r['T_total']} tokens ({r['T_rank']} per GPU), routed experts "
-                        f"sharded {256 // world} per GPU, uniform-random top-8 (seeded); dispatch and "
-                        "combine by the EP kernels over NVLink peer memory (BASELINE configs[3])",
+            "workload": f"one MoE block over {r['T_total']} tokens ({r['T_rank']} per GPU), routed experts' "
+                        f"gate/up sharded {256 // world} per GPU, down projections of each rank's own tokens "
+                        "at home (down-at-home mode), uniform-random top-8 (seeded); token rows out and "
+                        "activation rows back by the EP kernels over NVLink peer memory (BASELINE configs[3])",
             "n_gpus": world, "tokens_per_s": r["tokens_per_s"], "ms_per_block": r["ms_per_block"],
+            "sharded_tokens_per_s": r["sharded_tokens_per_s"],
+            "sharded_note": "fully sharded mode (down projections at the owners, fp32 result rows back), "
+                            "timed in the same run",
             "kernel_ms_max_over_ranks": r["kernel_ms"],
             "roofline": {"bound": "tensor", "kernel": "k_grouped (gate/up + down, per rank)", "achieved": tf,
                          "peak": tc_peak, "unit": "TFLOP/s", "frac": tf / tc_peak, "peak_kind": tc_kind},
             "dispatch_remote_bytes_rank0": r["dispatch_remote_bytes_rank0"],
+            "return_remote_bytes_rank0": r["return_remote_bytes_rank0"],
+            "sharded_return_remote_bytes_rank0": r["sharded_return_remote_bytes_rank0"],
             "ep_equal": r["ep_equal"], "ep_checked_tokens": r["ep_checked_tokens"],
-            "ep_check": "every rank's output for all of its tokens (two batches) equals the "
-                        "single-GPU block with all 256 experts on the same tokens and routing, "
+            "ep_check": "every rank's output for all of its tokens (two batches, both modes) equals "
+                        "the single-GPU block with all 256 experts on the same tokens and routing, "
                         "bit for bit (torch.equal), min over ranks",
             "one_gpu_tokens_per_s": r["one_gpu_tokens_per_s"],
             "efficiency_vs_one_gpu": r["efficiency_vs_one_gpu"],

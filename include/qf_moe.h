@@ -531,11 +531,20 @@ qf_status qf_ep_info(const qf_ep *ep, int32_t *experts_per_rank, int64_t *receiv
  * undefined; the EP group's counters no longer agree, so every rank destroys
  * its qf_ep and creates a new one.  The handle itself stays usable. */
 qf_status qf_ep_set_timeout_ms(qf_ep *ep, uint32_t ms);
+/* Down-at-home mode (enable 1; default 0, every rank the same): each owner
+ * runs only the gate/up of its experts and returns the fp16 activation rows
+ * (1 KB per routed row instead of 8 KB of fp32 results); every rank then runs
+ * the down projection of its own tokens with all 256 experts.  Needs
+ * layer->expert_bank to hold all 256 experts on every rank (the down
+ * projections are replicated); outputs are bit-identical either way.  No
+ * counterpart in the reference, which runs one GPU. */
+qf_status qf_ep_set_down_at_home(qf_ep *ep, int32_t enable);
 /* One MoE block over this rank's T tokens (T <= max_tokens), on the handle's
  * stream.  layer->expert_bank holds this rank's 256/world experts in order
- * (record i = expert rank * 256/world + i); router, coefficient and shared
- * expert are the full replicated weights.  routing: logit_bias, or a supplied
- * top-k (topk_idx/topk_w, global expert ids); record_of_pos is not supported. */
+ * (record i = expert rank * 256/world + i), or all 256 in down-at-home mode;
+ * router, coefficient and shared expert are the full replicated weights.
+ * routing: logit_bias, or a supplied top-k (topk_idx/topk_w, global expert
+ * ids); record_of_pos is not supported. */
 qf_status qf_moe_block_forward_ep(qf_ep *ep, const qf_moe_layer *layer, int32_t T,
                                   const uint16_t *x, const float *residual, float *out,
                                   const qf_routing *routing, int32_t *idx_out, float *w_out);

@@ -26,6 +26,15 @@
 //             and forms residual + c*shared + sum_k w_k y_k in router order --
 //             the same arithmetic as the single-GPU block, so the outputs are
 //             bit-identical to it.
+// Down-at-home mode (qf_ep_set_down_at_home; every rank holds all 256
+// experts): the owner runs only the gate/up GEMM and its epilogue stores each
+// fp16 activation row (1 KB) into the sending rank's activation area at the
+// row's send index; after every owner has signalled, each rank runs the down
+// GEMM over its own tokens' activation rows with all 256 experts (the
+// single-GPU block's down stage, same rows and tiles per expert), then the
+// same combine.  The NVLink return shrinks from 8 KB of fp32 results to 1 KB
+// of activations per routed row, at the cost of replicating the down
+// projections; the outputs stay bit-identical.
 // Counters are monotonically increasing (never reset) and every wait is bounded
 // (globaltimer deadline); an expired wait sets QF_ERR_TIMEOUT in the status word
 // and the kernel returns.
@@ -297,6 +306,15 @@ __global__ void __launch_bounds__(256) k_ep_expand(uint8_t* mine, size_t x_off, 
   }
 }
 
+// Down-at-home mode: wait (one thread) until every owner's activation rows
+// have landed here.  After an expired wait earlier in this call (q_rows < 0)
+// there is nothing to wait for.
+__global__ void k_ep_wait_done(uint8_t* mine, unsigned target, const int* q_rows, int* status, uint64_t wait_ns) {
+  if (threadIdx.x == 0 && *(volatile const int*)q_rows >= 0 &&
+      !wait_counter(sig(mine, kSigDone), target, wait_ns))
+    set_status(status, kStatusTimeout);
+}
+
 // The owner's result rows are written: tell every rank.
 __global__ void k_ep_signal_done(EpArgs a) {
   if (threadIdx.x == 0) {
@@ -367,7 +385,12 @@ size_t al256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 struct qf_ep {
   qf_moe* h = nullptr;
   int device = 0, rank = 0, world = 1, epr = 256, t_max = 0, sms = 0;
-  size_t rows_cap = 0, region_bytes = 0, x_off = 0, y_off = 0, ret_off = 0, tok_off = 0, src_off = 0, max_tiles = 0;
+  size_t rows_cap = 0, region_bytes = 0, x_off = 0, y_off = 0, ret_off = 0, tok_off = 0, src_off = 0, act_off = 0;
+  size_t max_tiles = 0, home_max_tiles = 0;
+  bool down_at_home = false;
+  int4* home_tiles = nullptr;
+  int* home_n_tiles = nullptr;
+  int* pmax_dev = nullptr;
   uint8_t* region = nullptr;
   uint8_t* peer[qf::kMaxRanks] = {};
   bool opened[qf::kMaxRanks] = {};
@@ -436,13 +459,18 @@ qf_status qf_ep_create(qf_moe* h, int32_t rank, int32_t world, int32_t max_token
   ep->ret_off = ep->y_off + al256(ep->rows_cap * qf::kHidden * 4);
   ep->src_off = ep->ret_off + al256(ep->rows_cap * 4);
   ep->tok_off = ep->src_off + al256(ep->rows_cap * 4);
-  ep->region_bytes = ep->tok_off + al256(static_cast<size_t>(world) * max_tokens * qf::kHidden * 2);
+  // down-at-home activation rows: [0, 8 max_tokens) routed by send row, then
+  // [8 max_tokens, +max_tokens) this rank's shared rows
+  ep->act_off = ep->tok_off + al256(static_cast<size_t>(world) * max_tokens * qf::kHidden * 2);
+  ep->region_bytes = ep->act_off + al256((P + max_tokens) * qf::kInter * 2);
+  ep->home_max_tiles = qf::grouped_max_tiles(max_tokens);
   ep->max_tiles = qf::grouped_max_tiles(max_tokens * world);
   size_t wsb = 0;
   wsb += al256(4 * (size_t)max_tokens * qf::kExperts) + al256(4 * (size_t)max_tokens);
   wsb += al256(4 * P) * 3 + al256(4 * (qf::kExperts + 1)) * 4 + al256(qf::dispatch_workspace_bytes(max_tokens));
   wsb += al256(16 * ep->max_tiles) + al256(16) + al256(4 * P) + al256(16);
   wsb += al256(ep->rows_cap * qf::kInter * 2);
+  wsb += al256(16 * ep->home_max_tiles) + al256(16) + al256(16);
   cudaError_t e = cudaDeviceGetAttribute(&ep->sms, cudaDevAttrMultiProcessorCount, h->device);
   if (e == cudaSuccess) e = cudaMalloc(&ep->region, ep->region_bytes);
   if (e == cudaSuccess) e = cudaMemset(ep->region, 0, qf::kSigBytes);
@@ -477,6 +505,19 @@ qf_status qf_ep_create(qf_moe* h, int32_t rank, int32_t world, int32_t max_token
   ep->loc_of_pos = reinterpret_cast<int*>(take(4 * P));
   ep->q_rows = reinterpret_cast<int*>(take(16));
   ep->act = reinterpret_cast<__half*>(take(ep->rows_cap * qf::kInter * 2));
+  ep->home_tiles = reinterpret_cast<int4*>(take(16 * ep->home_max_tiles));
+  ep->home_n_tiles = reinterpret_cast<int*>(take(16));
+  ep->pmax_dev = reinterpret_cast<int*>(take(16));
+  {
+    const int pm = static_cast<int>(P);  // first shared activation row in down-at-home mode
+    e = cudaMemcpy(ep->pmax_dev, &pm, sizeof(pm), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(ep->ws);
+      cudaFree(ep->region);
+      delete ep;
+      return qf::cuda_fail(h, e, "EP: allocation");
+    }
+  }
   ep->peer[rank] = ep->region;
   if (world == 1) ep->connected = true;
   *out = ep;
@@ -539,8 +580,10 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   qf::LayerW L;
   qf_status s = qf::layer_to_w(h, layer, &L);
   if (s != QF_OK) return s;
-  if (L.bank_records < static_cast<uint32_t>(ep->epr))
-    return qf::fail(h, QF_ERR_ARG, "EP: the bank must hold this rank's 256/world experts");
+  if (L.bank_records < static_cast<uint32_t>(ep->down_at_home ? qf::kExperts : ep->epr))
+    return qf::fail(h, QF_ERR_ARG,
+                    ep->down_at_home ? "EP: down-at-home mode needs all 256 experts in the bank"
+                                     : "EP: the bank must hold this rank's 256/world experts");
   if (T < 1 || T > ep->t_max) return qf::fail(h, QF_ERR_ARG, "EP: T must be in [1, max_tokens]");
   if (!x || !out || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
       (residual && (reinterpret_cast<uintptr_t>(residual) & 15)))
@@ -614,12 +657,41 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   out_route.rows_cap = static_cast<int>(ep->rows_cap);
   out_route.y_off = ep->y_off;
   out_route.ret = reinterpret_cast<const int*>(ep->region + ep->ret_off);
-  if (e == cudaSuccess)
-    e = qf::grouped_ffn(st, L, bf16, reinterpret_cast<const uint16_t*>(ep->region + ep->x_off), ep->rows_cap,
-                        ep->act, reinterpret_cast<float*>(ep->region + ep->y_off), nullptr, ep->tiles, ep->n_tiles,
-                        ep->max_tiles, ep->sms, h->d_status, &h->prof, &out_route);
-  if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: grouped experts");
-  qf::k_ep_signal_done<<<1, 32, 0, st>>>(a);
+  if (!ep->down_at_home) {
+    if (e == cudaSuccess)
+      e = qf::grouped_ffn(st, L, bf16, reinterpret_cast<const uint16_t*>(ep->region + ep->x_off), ep->rows_cap,
+                          ep->act, reinterpret_cast<float*>(ep->region + ep->y_off), nullptr, ep->tiles,
+                          ep->n_tiles, ep->max_tiles, ep->sms, h->d_status, &h->prof, &out_route);
+    if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: grouped experts");
+    qf::k_ep_signal_done<<<1, 32, 0, st>>>(a);
+  } else {
+    // the owner: gate/up of its experts (records rank * epr ... of the full
+    // bank), activation rows to their senders
+    qf::LayerW Lo = L;
+    Lo.bank = L.bank + static_cast<uint64_t>(ep->rank) * ep->epr * L.stride;
+    Lo.bank_records = static_cast<uint32_t>(ep->epr);
+    qf::EpOut act_route = out_route;
+    act_route.act_off = ep->act_off;
+    act_route.rows_cap = ep->t_max * (qf::kTopK + 1);
+    if (e == cudaSuccess)
+      e = qf::grouped_ffn_stages(st, Lo, bf16, reinterpret_cast<const uint16_t*>(ep->region + ep->x_off),
+                                 ep->rows_cap, ep->act, nullptr, nullptr, ep->tiles, ep->n_tiles, ep->max_tiles,
+                                 ep->sms, h->d_status, &h->prof, 1, &act_route, nullptr);
+    if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: grouped gate/up");
+    qf::k_ep_signal_done<<<1, 32, 0, st>>>(a);
+    // home: every owner's activation rows have landed; the down GEMM of this
+    // rank's own rows with all 256 experts, results at the send rows
+    qf::k_ep_wait_done<<<1, 32, 0, st>>>(ep->region, a.epoch * (unsigned)ep->world, ep->q_rows, h->d_status,
+                                         ep->wait_ns);
+    e = qf::tile_list(st, ep->counts, ep->offsets, T, ep->pmax_dev, ep->home_tiles, ep->home_n_tiles);
+    if (e == cudaSuccess)
+      e = qf::grouped_ffn_stages(st, L, bf16, nullptr, static_cast<size_t>(ep->t_max) * (qf::kTopK + 1),
+                                 reinterpret_cast<__half*>(ep->region + ep->act_off),
+                                 reinterpret_cast<float*>(ep->region + ep->y_off), nullptr, ep->home_tiles,
+                                 ep->home_n_tiles, ep->home_max_tiles, ep->sms, h->d_status, &h->prof, 2, nullptr,
+                                 nullptr);
+    if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: grouped down");
+  }
   {
     qf::ProfScope ps(&h->prof, qf::kKCombine, st);
     qf::k_ep_combine<<<T, 256, 0, st>>>(a, residual, ep->w, ep->coef, out);
@@ -627,6 +699,12 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
   e = cudaGetLastError();
   if (e != cudaSuccess) return qf::cuda_fail(h, e, "EP: combine");
   ep->epoch++;
+  return QF_OK;
+}
+
+qf_status qf_ep_set_down_at_home(qf_ep* ep, int32_t enable) {
+  if (!ep || (enable != 0 && enable != 1)) return QF_ERR_ARG;
+  ep->down_at_home = enable != 0;
   return QF_OK;
 }
 

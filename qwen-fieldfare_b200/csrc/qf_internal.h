@@ -155,11 +155,16 @@ cudaError_t prefill_block(cudaStream_t st, const LayerW& L, bool bf16, int T, co
 size_t grouped_max_tiles(int T);
 // Expert-parallel output of the down GEMM: ret[row] = (rank << 24) | r sends
 // result row `row` to row r of rank's result area (peer[rank] + y_off).
+// Expert-parallel epilogue routing: the result rows (down, MODE 1) or the
+// activation rows (gate/up, MODE 0, down-at-home mode) of received row r go to
+// rank ret[r] >> 24, row ret[r] & 0xFFFFFF of that rank's region (y_off /
+// act_off); rows_cap bounds the row.
 struct EpOut {
   uint8_t* peer[8];
   int n_peers;
   int rows_cap;
   size_t y_off;
+  size_t act_off;
   const int* ret;
 };
 cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, int T_shared,
@@ -167,6 +172,13 @@ cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, in
 cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
                         __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
                         size_t max_tiles, int sms, int* status, Prof* prof, const EpOut* ep);
+// The same GEMMs, stage by stage (bit 0: gate/up over `rows`, bit 1: down over
+// `act`; the maps of a stage that does not run are not built), with separate
+// epilogue routing per stage (ep0: activation rows, ep1: result rows).
+cudaError_t grouped_ffn_stages(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
+                               __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
+                               size_t max_tiles, int sms, int* status, Prof* prof, int stages,
+                               const EpOut* ep0, const EpOut* ep1);
 
 // ---- dispatch plan (qf_route.cu)
 size_t dispatch_workspace_bytes(int T);

@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       const bool shared = t.x == kExperts;
       const int n = t.z;
       const int pb = t.w + t.y;  // first row of the tile in the row space
-      if (MODE == 1) {
+      if (MODE == 1 || a.ep.ret) {
         for (int c = et; c < n; c += kEpiThreads) {
           if (!a.ep.ret) {
             sy->col_pos[i & 1][c] = (shared || !a.perm) ? pb + c : a.perm[pb + c];
@@ -784,13 +784,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
           }
           float* dst;
           {
-            // (rank << 24) | row: the row of that rank's result area, stored
-            // over NVLink while the following tiles run
+            // (rank << 24) | row: the row of that rank's result (MODE 1) or
+            // activation (MODE 0) area, stored over NVLink while the following
+            // tiles run
             const int code = a.ep.ret[pb + c];
             const int dr = code >> 24, row = code & 0xFFFFFF;
             if (dr < 0 || dr >= a.ep.n_peers || row >= a.ep.rows_cap) {
               set_status(a.status, kStatusDevice);
               dst = nullptr;
+            } else if (MODE == 0) {
+              dst = reinterpret_cast<float*>(a.ep.peer[dr] + a.ep.act_off + (size_t)row * kInter * 2);
             } else {
               dst = reinterpret_cast<float*>(a.ep.peer[dr] + a.ep.y_off) + (size_t)row * kHidden;
             }
@@ -817,11 +820,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
           tmem_ld16(tmem + lrow + hcol + c0, g);
           tmem_ld16(tmem + lrow + 128 + hcol + c0, v);
           tmem_ld_wait();
+          if (a.ep.ret) {
 #pragma unroll
-          for (int j = 0; j < 16; j++)
-            if (c0 + j < cend)
-              dst[(size_t)(c0 + j) * kInter] =
-                  __float2half_rn(silu_mul_fast(__uint_as_float(g[j]), __uint_as_float(v[j])));
+            for (int j = 0; j < 16; j++)
+              if (c0 + j < cend) {
+                __half* d = reinterpret_cast<__half*>(sy->col_row[i & 1][c0 + j]);
+                if (d) d[fp] = __float2half_rn(silu_mul_fast(__uint_as_float(g[j]), __uint_as_float(v[j])));
+              }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              if (c0 + j < cend)
+                dst[(size_t)(c0 + j) * kInter] =
+                    __float2half_rn(silu_mul_fast(__uint_as_float(g[j]), __uint_as_float(v[j])));
+          }
         }
       } else {
         const int f = part * 256 + eq * 32 + lane;
@@ -862,7 +874,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_grouped(const __grid_consta
       acc_use[1] += use1 ? 1u : 0u;
     }
     // peer stores are visible system-wide before the kernel that signals them runs
-    if (MODE == 1 && a.ep.ret) __threadfence_system();
+    if (a.ep.ret) __threadfence_system();
   } else if (warp < kLoadWarp) {
     // ---------------- MMA issue: warp 16 -> block 0 / acc0, warp 17 -> block 1 / acc1
     if (lane == 0) {
@@ -1153,18 +1165,20 @@ cudaError_t tile_list(cudaStream_t st, const int* counts, const int* offsets, in
   return cudaGetLastError();
 }
 
-cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
-                        __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
-                        size_t max_tiles, int sms, int* status, Prof* prof, const EpOut* ep) {
+cudaError_t grouped_ffn_stages(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
+                               __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
+                               size_t max_tiles, int sms, int* status, Prof* prof, int stages,
+                               const EpOut* ep0, const EpOut* ep1) {
   GemmArgs g0, g1;
-  if (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) || !encode_rows(&g1.map_rows, act, R, kInter, kTileRows) ||
-      !encode_rows(&g0.map_rows_small, rows, R, kHidden, kSmallTileRows) ||
-      !encode_rows(&g1.map_rows_small, act, R, kInter, kSmallTileRows))
+  if ((stages & 1) && (!encode_rows(&g0.map_rows, rows, R, kHidden, kTileRows) ||
+                       !encode_rows(&g0.map_rows_small, rows, R, kHidden, kSmallTileRows) ||
+                       !encode_weights(&g0, 0, 0, L.bank, L.bank_records, L.stride) ||
+                       !encode_weights(&g0, 1, 0, L.shared, 1, L.stride)))
     return cudaErrorInvalidValue;
-  if (!encode_weights(&g0, 0, 0, L.bank, L.bank_records, L.stride) ||
-      !encode_weights(&g0, 1, 0, L.shared, 1, L.stride) ||
-      !encode_weights(&g1, 0, 1, L.bank, L.bank_records, L.stride) ||
-      !encode_weights(&g1, 1, 1, L.shared, 1, L.stride))
+  if ((stages & 2) && (!encode_rows(&g1.map_rows, act, R, kInter, kTileRows) ||
+                       !encode_rows(&g1.map_rows_small, act, R, kInter, kSmallTileRows) ||
+                       !encode_weights(&g1, 0, 1, L.bank, L.bank_records, L.stride) ||
+                       !encode_weights(&g1, 1, 1, L.shared, 1, L.stride)))
     return cudaErrorInvalidValue;
   g0.L = g1.L = L;
   g0.perm = g1.perm = perm;
@@ -1173,18 +1187,18 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
   g0.act = g1.act = act;
   g0.y = g1.y = y;
   g0.status = g1.status = status;
-  g0.ep = EpOut{};
-  g1.ep = ep ? *ep : EpOut{};
-  const unsigned grid0 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<0>::PARTS);
-  {
+  g0.ep = ep0 ? *ep0 : EpOut{};
+  g1.ep = ep1 ? *ep1 : EpOut{};
+  if (stages & 1) {
+    const unsigned grid0 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<0>::PARTS);
     ProfScope ps(prof, kKGateUp, st);
     if (bf16)
       k_grouped<true, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
     else
       k_grouped<false, 0><<<grid0, kGemmThreads, kGemmSmem, st>>>(g0);
   }
-  const unsigned grid1 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<1>::PARTS);
-  {
+  if (stages & 2) {
+    const unsigned grid1 = (unsigned)std::min<size_t>((size_t)sms, max_tiles * Geo<1>::PARTS);
     ProfScope ps(prof, kKDown, st);
     if (bf16)
       k_grouped<true, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
@@ -1192,6 +1206,13 @@ cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint1
       k_grouped<false, 1><<<grid1, kGemmThreads, kGemmSmem, st>>>(g1);
   }
   return cudaGetLastError();
+}
+
+cudaError_t grouped_ffn(cudaStream_t st, const LayerW& L, bool bf16, const uint16_t* rows, size_t R,
+                        __half* act, float* y, const int* perm, const int4* tiles, const int* n_tiles,
+                        size_t max_tiles, int sms, int* status, Prof* prof, const EpOut* ep) {
+  return grouped_ffn_stages(st, L, bf16, rows, R, act, y, perm, tiles, n_tiles, max_tiles, sms, status, prof, 3,
+                            nullptr, ep);
 }
 
 // The routed experts of T tokens without the shared expert or the combine:

@@ -128,6 +128,7 @@ SIGNATURES = {
     "qf_ep_destroy": (None, [_P]),
     "qf_ep_info": (_S, [_P, C.POINTER(_I), C.POINTER(C.c_int64), C.POINTER(C.c_uint64)]),
     "qf_ep_set_timeout_ms": (_S, [_P, C.c_uint32]),
+    "qf_ep_set_down_at_home": (_S, [_P, C.c_int32]),
     "qf_moe_block_forward_ep": (_S, [_P, C.POINTER(MoELayerDesc), _I, _P, _P, _P,
                                      C.POINTER(RoutingDesc), _P, _P]),
     "qf_moe_profile_begin": (_S, [_P, _I, _I]),

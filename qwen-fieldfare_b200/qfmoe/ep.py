@@ -75,6 +75,12 @@ class ExpertParallel:
         """Deadline of each bounded wait on the other ranks (default 2 s)."""
         check(lib().qf_ep_set_timeout_ms(self.h, ms), self.ctx.h)
 
+    def set_down_at_home(self, enable: bool = True):
+        """Owners return fp16 activation rows and each rank runs the down
+        projection of its own tokens; the layer passed to forward() must then
+        hold all 256 experts (every rank the same mode)."""
+        check(lib().qf_ep_set_down_at_home(self.h, 1 if enable else 0), self.ctx.h)
+
     def local_layer(self, seed: int, layer: int) -> MoELayerWeights:
         """Seeded synthetic weights with this rank's experts in the bank."""
         return MoELayerWeights.synth(self.ctx, seed, layer, n_records=self.experts_per_rank,

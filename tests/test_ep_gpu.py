@@ -60,6 +60,32 @@ def test_ep_world1_equals_block(ctx, full_layer):
     ep.close()
 
 
+def test_ep_world1_down_at_home_equals_block(ctx, full_layer):
+    """Down-at-home mode: the owner returns activation rows and the home rank
+    runs the down projection with all 256 experts; same outputs bit for bit.
+    A bank with fewer than 256 experts is refused in this mode."""
+    from qfmoe import ExpertParallel, MoELayerWeights, QfError, block_forward, synth_hidden
+    ep = ExpertParallel(ctx, 0, 1, max_tokens=512)
+    ep.set_down_at_home(True)
+    bias = torch.from_numpy(zipf_bias()).cuda()
+    for i, T in enumerate((300, 512, 97)):
+        x = synth_hidden(SEED, 3000 + 1000 * i, T).cuda()
+        res = torch.randn((T, 2048), generator=torch.Generator().manual_seed(50 + i)).cuda()
+        out, idx, w = ep.forward(full_layer, x, res, logit_bias=bias if i else None, return_routing=True)
+        ref, ridx, rw = block_forward(ctx, full_layer, x, res, logit_bias=bias if i else None, return_routing=True)
+        ctx.check()
+        assert torch.equal(idx, ridx)
+        assert torch.equal(out, ref), (T, (out - ref).abs().max().item())
+    small = MoELayerWeights.synth(ctx, SEED, LAYER, n_records=128)
+    with pytest.raises(QfError):
+        ep.forward(small, synth_hidden(SEED, 0, 8).cuda())
+    ep.set_down_at_home(False)
+    # (T > 64: block_forward takes the prefill path, whose router the EP block uses)
+    x = synth_hidden(SEED, 9000, 128).cuda()
+    assert torch.equal(ep.forward(full_layer, x), block_forward(ctx, full_layer, x))
+    ep.close()
+
+
 def test_ep_world1_small_batch_vs_oracle(ctx, full_layer):
     from qfmoe import ExpertParallel, synth_hidden
     ep = ExpertParallel(ctx, 0, 1, max_tokens=16)
@@ -126,10 +152,13 @@ def _worker(rank, world, port, q):
         full = Q.MoELayerWeights.synth(ctx, SEED, LAYER)
         bias = torch.from_numpy(zipf_bias()).cuda()
         equal = []
-        for step in range(4):
+        for step in range(6):
+            # steps 4, 5: down-at-home mode (all 256 experts on each rank)
+            if step == 4:
+                ep.set_down_at_home(True)
             x = Q.synth_hidden(SEED, 10000 * step + rank * T, T).cuda()
             res = torch.randn((T, 2048), generator=torch.Generator().manual_seed(100 * step + rank)).cuda()
-            out = ep.forward(local, x, res, logit_bias=bias if step % 2 else None)
+            out = ep.forward(local if step < 4 else full, x, res, logit_bias=bias if step % 2 else None)
             ref = Q.block_forward(ctx, full, x, res, logit_bias=bias if step % 2 else None)
             ctx.check()
             equal.append(bool(torch.equal(out, ref)))

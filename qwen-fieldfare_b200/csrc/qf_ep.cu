@@ -315,6 +315,15 @@ __global__ void k_ep_wait_done(uint8_t* mine, unsigned target, const int* q_rows
     set_status(status, kStatusTimeout);
 }
 
+// Down-at-home mode, before the home tile list: the shared rows start at
+// `pmax`, and after an expired wait (q_rows < 0) the list is empty (no routed
+// counts, a negative shared base), so the home down GEMM does no work.
+__global__ void k_ep_home_guard(const int* q_rows, int* counts, int* home_base, int pmax) {
+  const bool abort = *(volatile const int*)q_rows < 0;
+  if (abort) counts[threadIdx.x] = 0;
+  if (threadIdx.x == 0) *home_base = abort ? -1 : pmax;
+}
+
 // The owner's result rows are written: tell every rank.
 __global__ void k_ep_signal_done(EpArgs a) {
   if (threadIdx.x == 0) {
@@ -508,16 +517,7 @@ qf_status qf_ep_create(qf_moe* h, int32_t rank, int32_t world, int32_t max_token
   ep->home_tiles = reinterpret_cast<int4*>(take(16 * ep->home_max_tiles));
   ep->home_n_tiles = reinterpret_cast<int*>(take(16));
   ep->pmax_dev = reinterpret_cast<int*>(take(16));
-  {
-    const int pm = static_cast<int>(P);  // first shared activation row in down-at-home mode
-    e = cudaMemcpy(ep->pmax_dev, &pm, sizeof(pm), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-      cudaFree(ep->ws);
-      cudaFree(ep->region);
-      delete ep;
-      return qf::cuda_fail(h, e, "EP: allocation");
-    }
-  }
+  // (pmax_dev: the home tile list's shared base, set per call by k_ep_home_guard)
   ep->peer[rank] = ep->region;
   if (world == 1) ep->connected = true;
   *out = ep;
@@ -683,6 +683,7 @@ qf_status qf_moe_block_forward_ep(qf_ep* ep, const qf_moe_layer* layer, int32_t 
     // rank's own rows with all 256 experts, results at the send rows
     qf::k_ep_wait_done<<<1, 32, 0, st>>>(ep->region, a.epoch * (unsigned)ep->world, ep->q_rows, h->d_status,
                                          ep->wait_ns);
+    qf::k_ep_home_guard<<<1, qf::kExperts, 0, st>>>(ep->q_rows, ep->counts, ep->pmax_dev, ep->t_max * qf::kTopK);
     e = qf::tile_list(st, ep->counts, ep->offsets, T, ep->pmax_dev, ep->home_tiles, ep->home_n_tiles);
     if (e == cudaSuccess)
       e = qf::grouped_ffn_stages(st, L, bf16, nullptr, static_cast<size_t>(ep->t_max) * (qf::kTopK + 1),

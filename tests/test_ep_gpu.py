@@ -193,7 +193,7 @@ def test_ep_two_gpus_equals_single_gpu_block():
         assert all(equal), (r, equal)
 
 
-def _timeout_worker(rank, world, port, q, dev):
+def _timeout_worker(rank, world, port, q, dev, down_at_home=False):
     """Rank 1 creates and connects, then leaves the group: it never calls
     forward, but keeps its exported region alive (rank 0 stores into it) until
     rank 0 has finished.  Rank 0 calls forward with a 50 ms deadline."""
@@ -221,10 +221,14 @@ def _timeout_worker(rank, world, port, q, dev):
             q.put((rank, None, None))
             return
         ep.set_timeout_ms(50)
-        local = ep.local_layer(SEED, LAYER)
+        if down_at_home:
+            ep.set_down_at_home(True)
+            layer = Q.MoELayerWeights.synth(ctx, SEED, LAYER)
+        else:
+            layer = ep.local_layer(SEED, LAYER)
         x = Q.synth_hidden(SEED, 0, T).cuda()
         t0 = time.time()
-        ep.forward(local, x)
+        ep.forward(layer, x)
         torch.cuda.synchronize()
         elapsed = time.time() - t0
         try:
@@ -254,7 +258,8 @@ def _timeout_worker(rank, world, port, q, dev):
         dist.destroy_process_group()
 
 
-def test_ep_missing_rank_times_out_and_the_handle_recovers():
+@pytest.mark.parametrize("down_at_home", [False, True], ids=["sharded", "down_at_home"])
+def test_ep_missing_rank_times_out_and_the_handle_recovers(down_at_home):
     """A rank that never arrives: rank 0's bounded waits expire after the 50 ms
     deadline, qf_moe_check reports QF_ERR_TIMEOUT, the call's GEMMs do no work,
     and a following world-1 call on the same handle equals the single-GPU block.
@@ -266,7 +271,7 @@ def test_ep_missing_rank_times_out_and_the_handle_recovers():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_timeout_worker, args=(r, world, port, q, r if two else 0))
+    procs = [ctx.Process(target=_timeout_worker, args=(r, world, port, q, r if two else 0, down_at_home))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -8,11 +8,11 @@ expert-parallel block does across `world` ranks of a torch.distributed group:
      row  sum_{owner's experts e' < e} total(e') + sum_{ranks s < me} count_s(e)
           + (rank of the row among my rows of e)
      (expert-major, then source rank, then (token, k)); on the wire a token
-     row crosses once per owner (sent by the token's lowest k with an expert
-     there, into the owner's token area at row  source rank * t_max + token),
-     each routed row carries the index of that token row, and the owner
-     expands the token area into its receive rows (qf_ep.cu k_ep_dispatch,
-     k_ep_expand);
+     row crosses once per owner: into the receive row of the token's lowest k
+     with an expert there, which the owner's first-row map records at
+     source rank * t_max + token; the token's other rows there carry that
+     map index and the owner copies them from the first row (qf_ep.cu
+     k_ep_dispatch, k_ep_expand);
   4. owners evaluate their experts on the received rows;
   5. each rank pulls its rows' results back and combines them in router order.
 The per-token math is qfo_block's, so the outputs equal the single-process
@@ -62,8 +62,8 @@ def ep_block(seed: int, layer: int, x16: np.ndarray, rank: int, world: int, grou
     ts = [None] * world
     dist.all_gather_object(ts, T, group=group)
     t_max = max(ts)
-    send_tok = {d: [] for d in range(world)}  # (token-area row, token row): once per (token, owner)
-    send_idx = {d: [] for d in range(world)}  # (receive row, token-area row): one per routed row
+    send_row = {d: [] for d in range(world)}  # (receive row, map index, token row): once per (token, owner)
+    send_idx = {d: [] for d in range(world)}  # (receive row, map index): the other routed rows
     loc = np.zeros((T * O.TOPK, 2), np.int64)
     for j, pos in enumerate(perm):
         e = int(flat[pos])
@@ -71,25 +71,28 @@ def ep_block(seed: int, layer: int, x16: np.ndarray, rank: int, world: int, grou
         t, k = divmod(int(pos), O.TOPK)
         row = int(base[e] + j - offsets[e])
         trow = rank * t_max + t
-        send_idx[d].append((row, trow))
         if all(int(flat[t * O.TOPK + kk]) // epr != d for kk in range(k)):
-            send_tok[d].append((trow, x16[t]))
+            send_row[d].append((row, trow, x16[t]))
+        else:
+            send_idx[d].append((row, trow))
         loc[pos] = (d, row)
-    toks = [None] * world
+    firsts = [None] * world
     idxs = [None] * world
-    dist.all_gather_object(toks, send_tok, group=group)
+    dist.all_gather_object(firsts, send_row, group=group)
     dist.all_gather_object(idxs, send_idx, group=group)
-    area = {}
-    for src in toks:
-        for trow, xr in src[rank]:
-            if trow in area:
-                raise AssertionError("a token row crossed twice to the same owner")
-            area[trow] = xr
     recv = np.zeros((q, O.HIDDEN), np.uint16)
     placed = np.zeros(q, np.int64)
+    first_row = {}
+    for src in firsts:
+        for row, trow, xr in src[rank]:
+            if trow in first_row:
+                raise AssertionError("a token row crossed twice to the same owner")
+            first_row[trow] = row
+            recv[row] = xr
+            placed[row] += 1
     for src in idxs:
         for row, trow in src[rank]:
-            recv[row] = area[trow]  # the expand step
+            recv[row] = recv[first_row[trow]]  # the expand step
             placed[row] += 1
     if not (placed == 1).all():
         raise AssertionError("owner rows are not a bijection")

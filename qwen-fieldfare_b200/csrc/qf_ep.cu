@@ -10,11 +10,13 @@
 //             also means every rank has finished reading the previous call's
 //             buffers), and stores each token row (fp16, already in the grouped
 //             GEMM's K order) over NVLink ONCE per owner rank that holds any of
-//             its 8 experts, into the owner's token area (row source rank x
-//             max_tokens + token); each routed row sends only the 4-byte index
-//             of that token row to its receive row, which lands expert-major,
-//             then by source rank, then in the source's (token, k) order;
-//   expand    the owner copies the token rows into its receive rows (local
+//             its 8 experts: into the receive row of the token's first position
+//             (lowest k) with an expert there, recording that row in the
+//             owner's first-row map (source rank x max_tokens + token); the
+//             token's other positions on that owner send only the 4-byte map
+//             index; receive rows land expert-major, then by source rank, then
+//             in the source's (token, k) order;
+//   expand    the owner copies each such duplicate from its first row (local
 //             HBM), so its grouped GEMM reads contiguous rows of its own memory;
 //   GEMMs     the owner runs the grouped tcgen05 gate/up and down GEMMs over
 //             its received rows plus its own tokens' shared-expert rows; the
@@ -113,8 +115,8 @@ struct EpArgs {
   uint8_t* peer[kMaxRanks];  // exported region of each rank (this rank's own included)
   size_t x_off, y_off;   // receive rows / result rows inside a region
   size_t ret_off;        // int [rows_cap]: return address of each received row
-  size_t tok_off;        // token area: [world][t_max] fp16 rows, one per (source rank, token)
-  size_t src_off;        // int [rows_cap]: token-area row of each received routed row
+  size_t tok_off;        // first-row map: int [world][t_max], the receive row of each (source rank, token)
+  size_t src_off;        // int [rows_cap]: map index of a duplicate received row, -1 for a first row
   int t_max;             // tokens per rank of the token area
   int pmax;              // result rows [0, pmax) are send rows, [pmax, pmax + T) shared rows
   int* loc_of_pos;       // [P] send row of each position (its result row here)
@@ -231,22 +233,26 @@ __global__ void __launch_bounds__(kDispThreads) k_ep_dispatch(const __grid_const
         continue;
       }
       const int trow = a.rank * a.t_max + src_t;
-      if (lane == 0) {
-        // where the owner's down GEMM sends this row's result, and which
-        // token row the owner expands into it
-        reinterpret_cast<int*>(a.peer[d] + a.ret_off)[row] = (a.rank << 24) | j;
-        reinterpret_cast<int*>(a.peer[d] + a.src_off)[row] = trow;
-      }
-      // the token row crosses once per owner: sent by the token's first
-      // position (lowest k) with an expert on that owner
+      // the token row crosses once per owner: the token's first position
+      // (lowest k) with an expert on that owner carries it (its 8 expert ids
+      // in two 16-byte loads)
+      const int4 i0 = __ldg(reinterpret_cast<const int4*>(a.idx) + 2 * src_t);
+      const int4 i1 = __ldg(reinterpret_cast<const int4*>(a.idx) + 2 * src_t + 1);
+      const int es[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
       bool first = true;
       const int k = pos & 7;
-      for (int kk = 0; kk < k; kk++) {
-        const int e2 = a.idx[(src_t << 3) + kk];
-        first &= !(e2 >= 0 && e2 < kExperts && e2 / a.epr == d);
+#pragma unroll
+      for (int kk = 0; kk < 7; kk++)
+        first &= !(kk < k && es[kk] >= 0 && es[kk] < kExperts && es[kk] / a.epr == d);
+      if (lane == 0) {
+        // where the owner's down GEMM sends this row's result; a duplicate
+        // names the map entry of the row its bytes are copied from
+        reinterpret_cast<int*>(a.peer[d] + a.ret_off)[row] = (a.rank << 24) | j;
+        reinterpret_cast<int*>(a.peer[d] + a.src_off)[row] = first ? -1 : trow;
+        if (first) reinterpret_cast<int*>(a.peer[d] + a.tok_off)[trow] = row;
       }
       if (!first) continue;
-      dst = reinterpret_cast<uint4*>(a.peer[d] + a.tok_off) + static_cast<size_t>(trow) * (kHidden / 8);
+      dst = reinterpret_cast<uint4*>(a.peer[d] + a.x_off) + static_cast<size_t>(row) * (kHidden / 8);
     } else {
       d = a.rank;
       src_t = j - a.P;
@@ -282,25 +288,28 @@ __global__ void k_ep_wait_rows(uint8_t* mine, unsigned target, const int* q_rows
     set_status(status, kStatusTimeout);
 }
 
-// Owner: receive row r < q_rows (routed) <- its token-area row (local copy,
-// one warp per row).  Nothing after an expired wait (q_rows < 0).
+// Owner: each duplicate receive row r < q_rows (routed) <- the first row of
+// its (source rank, token), named by the first-row map (local copy, one warp
+// per row).  Nothing after an expired wait (q_rows < 0).
 __global__ void __launch_bounds__(256) k_ep_expand(uint8_t* mine, size_t x_off, size_t tok_off, size_t src_off,
                                                    int tok_rows, const int* q_rows, int* status) {
   const int q = *q_rows;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int nw = (gridDim.x * blockDim.x) >> 5;
   const int* src = reinterpret_cast<const int*>(mine + src_off);
-  const uint4* tok = reinterpret_cast<const uint4*>(mine + tok_off);
+  const int* first_row = reinterpret_cast<const int*>(mine + tok_off);
   uint4* rows = reinterpret_cast<uint4*>(mine + x_off);
   for (int r = warp; r < q; r += nw) {
     const int t = __ldcg(src + r);
-    if (t < 0 || t >= tok_rows) {
+    if (t < 0) continue;  // a first row: its bytes came over NVLink
+    const int f = t < tok_rows ? __ldcg(first_row + t) : -1;
+    if (f < 0 || f >= q) {
       if (lane == 0) set_status(status, kStatusDevice);
       continue;
     }
     uint4 v[kHidden / 8 / 32];
 #pragma unroll
-    for (int i = 0; i < kHidden / 8 / 32; i++) v[i] = __ldcg(tok + static_cast<size_t>(t) * (kHidden / 8) + lane + 32 * i);
+    for (int i = 0; i < kHidden / 8 / 32; i++) v[i] = __ldcg(rows + static_cast<size_t>(f) * (kHidden / 8) + lane + 32 * i);
 #pragma unroll
     for (int i = 0; i < kHidden / 8 / 32; i++) rows[static_cast<size_t>(r) * (kHidden / 8) + lane + 32 * i] = v[i];
   }
@@ -470,7 +479,7 @@ qf_status qf_ep_create(qf_moe* h, int32_t rank, int32_t world, int32_t max_token
   ep->tok_off = ep->src_off + al256(ep->rows_cap * 4);
   // down-at-home activation rows: [0, 8 max_tokens) routed by send row, then
   // [8 max_tokens, +max_tokens) this rank's shared rows
-  ep->act_off = ep->tok_off + al256(static_cast<size_t>(world) * max_tokens * qf::kHidden * 2);
+  ep->act_off = ep->tok_off + al256(static_cast<size_t>(world) * max_tokens * 4);
   ep->region_bytes = ep->act_off + al256((P + max_tokens) * qf::kInter * 2);
   ep->home_max_tiles = qf::grouped_max_tiles(max_tokens);
   ep->max_tiles = qf::grouped_max_tiles(max_tokens * world);
